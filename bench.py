@@ -1,0 +1,280 @@
+#!/usr/bin/env python
+"""Benchmark of the scene-packed attention hot path on B200 (BASELINE.json metric: scene-packed attention TFLOP/s per
+GPU). One step = one scene-attention layer of BASELINE cfg2 (HunyuanVideo-1.5 shape: 4 scenes of [8, 6, 10, 7] latent
+frames, 1590 tokens per frame, 128 text tokens per scene, frame memory {0, 8, 14, 24}, 16 heads x 128, bf16):
+the gather/pack launch (K and V of every segment) plus the attention launches (video queries, text queries), inputs
+resident in HBM. Useful FLOPs per step = sum over segments of 4 * lq * lk * H * D (experiments/kernel_breakdown.py:101
+of the reference) = 7.187 TFLOP.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's CPU path (oracle/cpu_path.py: the reference processor with per-segment fp32
+SDPA in place of FlashAttention) on the host cores, rank 0 only. Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG2 = dict(lengths=[8, 6, 10, 7], T=1590, text=128, heads=16, dim=128, memory=[0, 8, 14, 24])
+METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
+
+
+def cfg2_layout():
+    from onereel_b200.layout import SceneLayout
+    lay = SceneLayout(CFG2['lengths'], halo=0)
+    lay.extra = {j: [f for f in CFG2['memory'] if not lo <= f < hi] for j, (lo, hi) in enumerate(lay.ranges)}
+    return lay
+
+
+def peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d['bf16_tflops'], d.get('bf16_tflops_sustained'), d['hbm_gbs'], 'measured'
+    return 1590.0, 1400.0, 6650.0, 'fallback'
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region"""
+    Q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, Path(f'/tmp/orl_clocks_{os.getpid()}.csv')
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.Q}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return None
+        rows = [r.split(', ') for r in self.path.read_text().strip().splitlines() if r.count(',') >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
+        mx = max(float(r[2]) for r in rows)
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == 'Active'})
+        load = [s for s in sm if s > 0.5 * mx] or sm
+        self.path.unlink(missing_ok=True)
+        return dict(sm_mhz=float(np.median(load)), sm_max_mhz=mx, reasons=reasons, samples=len(rows))
+
+
+def dist_env():
+    return int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1)), int(os.environ.get('LOCAL_RANK', 0))
+
+
+def cpu_baseline(steps=1, warmup=0, target_s=3.0):
+    """the reference CPU path on a bounded sample of cfg2 (every `sample`-th query row of every segment, all keys)"""
+    from oracle import cpu_path, layout_oracle as LO
+    lay = LO.Layout(CFG2['lengths'], halo=0, extra={j: [f for f in CFG2['memory'] if not lo <= f < hi]
+                                                   for j, (lo, hi) in enumerate(LO.Layout(CFG2['lengths']).ranges())})
+    counts = [CFG2['text']] * len(CFG2['lengths'])
+    H, Dh = CFG2['heads'], CFG2['dim']
+    probe_t, probe_f, _ = cpu_path.time_cpu(lay, CFG2['T'], counts, H, Dh, sample=512, repeats=1)
+    full = 7.187e12
+    sample = max(1, int(round(full / (probe_f / probe_t) / target_s)))
+    ts, fl = [], 0.0
+    for i in range(warmup + steps):
+        t, fl, threads = cpu_path.time_cpu(lay, CFG2['T'], counts, H, Dh, sample=sample, repeats=1, seed=i)
+        if i >= warmup:
+            ts.append(t)
+    t = float(np.median(ts))
+    return dict(value=fl / t / 1e12, unit='TFLOP/s', cores=threads, kind='port',
+                sample=f'cfg2 layer, every {sample}th query row of every segment with all its keys '
+                       f'({fl / 1e12:.3f} TFLOP of the 7.187), fp32 torch SDPA per segment, median of {len(ts)}'), t
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    cb, t = cpu_baseline(steps=args.steps, warmup=args.warmup)
+    line = dict(impl='reference', metric=METRIC, value=cb['value'], unit='TFLOP/s', n_gpus=args.gpus,
+                steps=args.steps, warmup=args.warmup, ms_per_step=t * 1e3, higher_is_better=True, scaling='weak',
+                vs_baseline=None, dtype='f32', data='synthetic',
+                config=dict(workload='cfg2 scene-attention layer (reference CPU path, bounded sample)',
+                            layout=CFG2), cpu_baseline=cb,
+                e2e=dict(value=cb['value'], unit='TFLOP/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def make_inputs(lay, T, counts, H, Dh, dev, seed=0):
+    """Q/K RMS-normed over D from N(0, 1) (unit weight), V ~ N(0, 1), seeded on the CPU (BASELINE cfg2)"""
+    g = torch.Generator().manual_seed(seed)
+    L, Nt = lay.n_frames * T, sum(counts)
+
+    def qk(n):
+        x = torch.randn(n, H, Dh, generator=g)
+        return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    q, k = qk(L), qk(L)
+    v = torch.randn(L, H, Dh, generator=g).to(torch.bfloat16)
+    eq, ek = qk(Nt), qk(Nt)
+    ev = torch.randn(Nt, H, Dh, generator=g).to(torch.bfloat16)
+    return [x.to(dev) for x in (q, k, v, eq, ek, ev)]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    if args.impl == 'reference':
+        return run_reference(args)
+
+    from onereel_b200 import attention as A
+    from onereel_b200 import scene as S
+    from onereel_b200.csrc.build import build
+    rank, world, local = dist_env()
+    build()
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
+
+    lay = cfg2_layout()
+    T, H, Dh = CFG2['T'], CFG2['heads'], CFG2['dim']
+    counts = [CFG2['text']] * lay.n_scenes
+    L = lay.n_frames * T
+    q, k, v, eq, ek, ev = make_inputs(lay, T, counts, H, Dh, dev, seed=rank)
+    mine = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
+    segs = S.scene_segments(lay, T, counts, mine, set(range(lay.n_scenes)), (0, L))
+    plan = S.ScenePlan(segs, row_bytes=H * Dh * 2, heads=H, device=dev)
+    flops = sum(4.0 * a * b * H * Dh for a, b in zip(plan.lq, plan.lk))
+    ov, ot = torch.empty_like(q), torch.zeros_like(eq)
+    kp = q.new_empty(plan.n_keys, H, Dh)
+    vp = q.new_empty(plan.n_keys, H, Dh)
+    stream = torch.cuda.current_stream(dev)
+    ev_attn = []
+
+    def step(record=False):
+        plan.pack_kv(k, v, ek, ev, out=(kp, vp))
+        if record:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+        S.attend_segments(plan, q, eq, kp, vp, ov, ot)
+        if record:
+            b.record(stream)
+            ev_attn.append((a, b))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    A.check()
+
+    with Clocks(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(record=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    A.check()
+    ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_attn]))
+
+    # end to end through the public API with host buffers: H2D of the layer's q/k/v/eq/ek/ev from pinned memory,
+    # the step, D2H of the outputs, every step inside the timed region
+    host_in = [x.cpu().pin_memory() for x in (q, k, v, eq, ek, ev)]
+    host_out = [torch.empty(ov.shape, dtype=ov.dtype, pin_memory=True),
+                torch.empty(ot.shape, dtype=ot.dtype, pin_memory=True)]
+    dev_in = [torch.empty_like(x) for x in (q, k, v, eq, ek, ev)]
+
+    def e2e_step():
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        dq, dk, dv, deq, dek, dev_ = dev_in
+        kp2, vp2 = plan.pack_kv(dk, dv, dek, dev_, out=(kp, vp))
+        S.attend_segments(plan, dq, deq, kp2, vp2, ov, ot)
+        host_out[0].copy_(ov, non_blocking=True)
+        host_out[1].copy_(ot, non_blocking=True)
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_steps = max(3, args.steps // 2)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    A.check()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, attn_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    peak_burst, peak_sus, hbm, peak_kind = peaks()
+    achieved = flops / (attn_ms * 1e-3) / 1e12
+    cb = None
+    if not args.no_cpu_baseline:
+        cb, _ = cpu_baseline()
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = sum(x.numel() * x.element_size() for x in host_out)
+    line = dict(metric=METRIC, value=world * flops / (ms * 1e-3) / 1e12, unit='TFLOP/s', n_gpus=world,
+                steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling='weak',
+                vs_baseline=None, dtype='bf16', data='synthetic (seeded; Q/K RMS-normed N(0,1), V N(0,1))',
+                config=dict(workload='cfg2: one HunyuanVideo-1.5-shaped scene-attention layer (pack K/V + attention)',
+                            layout=CFG2, segments=len(plan.segs), sum_q=sum(plan.lq), sum_k=sum(plan.lk),
+                            useful_tflop_per_step=flops / 1e12, parallelism=f'replicas x{world}' if world > 1 else 'single',
+                            l2='inputs larger than L2 (q/k/v 203 MB each, packed K/V 486 MB each)'),
+                e2e=dict(value=world * flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s', ms_per_step=e2e_ms,
+                         h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
+                roofline=dict(bound='tensor', achieved=achieved, peak=peak_burst, unit='TFLOP/s',
+                              frac=achieved / peak_burst, traffic=None,
+                              kernel='attn_fwd_kernel<128> (video + text launches per step)',
+                              peak_source=f'{peak_kind} bf16 burst'),
+                gpu_launches=3 * args.steps, clocks=clk.summary(), cpu_baseline=cb)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

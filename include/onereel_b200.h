@@ -1,0 +1,115 @@
+/* onereel_b200 — C ABI of the B200-native scene-packed attention path.
+ *
+ * A drop-in for the device work of OneReel's scene attention (reference repository UIUC-MLSys/OneReel):
+ *   - orl_attn_plan / orl_attn_fwd replace the FlashAttention varlen call of src/onereel/attention.py:39-53
+ *     (`varlen`, `varlen_lse`), which `packed` / `packed_lse` (attention.py:56-71) and the scene processors
+ *     (src/onereel/models/hunyuan15.py:212-303, src/onereel/models/wan.py:110-152) reach;
+ *   - orl_pack replaces the torch.cat row copies that assemble every packed segment's q / k / v
+ *     (attention.py:60-61, 69; hunyuan15.py:164, 168, 225; comm.py:200 `HaloExchange.rows`) and the output
+ *     scatter back to token rows (hunyuan15.py:231-235, wan.py:117-118), and emits cu_seqlens (attention.py:28-29);
+ *   - orl_lse_merge replaces the log-sum-exp merge of two partial results (hunyuan15.py:274-276, ring.py:63-70);
+ *   - the planner entry points restate comm.py:18-112 (Algorithm 1, exchange sets, Eq. 2) natively.
+ *
+ * Conventions: device pointers are CUDA global memory on the current device; `stream` is a cudaStream_t (NULL =
+ * legacy default stream). Every entry point returns 0 (ORL_OK) or a negative ORL_ERR_* code and never throws.
+ * No entry point allocates device memory; scratch (work lists, error words) is passed in by the caller.
+ * Tensors are row-major: q [nq, heads, head_dim], k / v [nk, heads, head_dim], bf16, rows contiguous.
+ */
+#ifndef ONEREEL_B200_H
+#define ONEREEL_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define ORL_API __attribute__((visibility("default")))
+#else
+#define ORL_API
+#endif
+
+#define ORL_OK 0
+#define ORL_ERR_ARG (-1)          /* invalid argument (null pointer, negative size, inconsistent cu_seqlens) */
+#define ORL_ERR_ALIGN (-2)        /* a pointer or row size is not 16-byte aligned */
+#define ORL_ERR_UNSUPPORTED (-3)  /* head_dim not in {64, 128} */
+#define ORL_ERR_DRIVER (-4)       /* cuTensorMapEncodeTiled unavailable */
+#define ORL_ERR_TENSOR_MAP (-5)   /* the driver rejected a tensor map */
+#define ORL_ERR_LAUNCH (-6)       /* kernel launch failed */
+#define ORL_ERR_CAPACITY (-7)     /* a caller buffer is too small */
+
+/* One attention work item: up to 256 query rows of one segment and one head. */
+typedef struct orl_attn_work {
+  int32_t q_row0; /* first packed query row */
+  int32_t q_len;  /* query rows in this item, 1..256 */
+  int32_t k_row0; /* first packed key row of the segment */
+  int32_t k_len;  /* keys of the segment (0 gives a zero output and LSE -inf) */
+  int32_t head;
+  int32_t seg;    /* segment index, for diagnostics */
+  int32_t pad0, pad1;
+} orl_attn_work;
+
+/* Library version string. */
+ORL_API const char* orl_version(void);
+
+/* Message for an ORL_ERR_* code. */
+ORL_API const char* orl_error_string(int code);
+
+/* Bits the kernels set in the caller's error word when a bounded wait gave up (the kernel then winds down). */
+ORL_API int orl_error_bits_describe(int bits, char* buf, int cap);
+
+/* Work list of a packed varlen call: replaces the scheduling FlashAttention does internally for
+ * attention.py:39-43. cu_q / cu_k: HOST int32 [n_seg + 1] (attention.py:28-29 cu_seqlens). Writes up to
+ * `capacity` items (largest key range first; items of one segment and head adjacent) and returns their count.
+ * If `work` is NULL or too small, returns -(needed + 1000) so the caller can size the buffer. */
+ORL_API int orl_attn_plan(const int32_t* cu_q, const int32_t* cu_k, int n_seg, int heads, orl_attn_work* work,
+                          int capacity);
+
+/* As orl_attn_plan, with each segment's query and key rows given as (start, length): key ranges may overlap and
+ * need not be in order, so contiguous per-scene key ranges are read in place without a pack. Replaces the FA3
+ * `cu_seqlens_k` offsets + `seqused_k` call of attention.py:74-84 (`overlapping_ranges`). HOST int32 [n_seg] each. */
+ORL_API int orl_attn_plan_ranges(const int32_t* q_start, const int32_t* q_len, const int32_t* k_start,
+                                 const int32_t* k_len, int n_seg, int heads, orl_attn_work* work, int capacity);
+
+/* Packed varlen attention forward (attention.py:39-53 `varlen` / `varlen_lse`): out = softmax(q k^T * scale) v per
+ * segment, out [nq, heads, head_dim] bf16; lse (optional, may be NULL) [heads, nq] fp32 natural-log LSE.
+ * work_dev: the plan's items in device memory; err_dev: a device int the kernel ORs timeout bits into (the caller
+ * zeroes it; nonzero after the call means the result is invalid). head_dim 64 or 128. */
+ORL_API int orl_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse, long long nq, long long nk,
+                 int heads, int head_dim, float scale, const orl_attn_work* work_dev, int n_items, int* err_dev,
+                 void* stream);
+
+/* One row-range copy of a pack: `nbytes` from base[src_slot] + src_off to base[dst_slot] + dst_off. */
+typedef struct orl_copy_run {
+  int32_t src_slot; /* index into src_bases */
+  int32_t dst_slot; /* index into dst_bases */
+  int64_t src_off;  /* bytes */
+  int64_t dst_off;  /* bytes */
+  int64_t vec0;     /* first 16-byte vector of this run in the pack (prefix sum, filled by orl_pack_prepare) */
+} orl_copy_run;
+
+/* Fills runs[i].vec0 (prefix sums of nbytes[i] / 16) and returns the pack's total 16-byte vectors, or an error if
+ * a size or offset is not a multiple of 16. nbytes: HOST int64 [n_runs]. */
+ORL_API long long orl_pack_prepare(orl_copy_run* runs, const int64_t* nbytes, int n_runs);
+
+/* Gather/pack kernel: executes the prepared run table (device copy, runs_dev [n_runs]) for `n_planes` planes at
+ * once (e.g. K and V share one run table): plane p reads src_bases[p * n_slots + slot] and writes
+ * dst_bases[p * n_slots + slot]. Coalesced 16-byte vector copies, HBM-bound. When cu_out_dev is not NULL, also
+ * writes cu_seqlens: cu_out_dev[0 .. n_seg] = [0, cumsum(seg_len_dev)] (int32, attention.py:28-29).
+ * At most 8 slots and 3 planes. */
+ORL_API int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_vecs, int n_planes, int n_slots,
+             const void* const* src_bases, void* const* dst_bases, const int32_t* seg_len_dev, int n_seg,
+             int32_t* cu_out_dev, void* stream);
+
+/* Log-sum-exp merge of two partial attention results over disjoint key sets (hunyuan15.py:274-276, ring.py:63-70):
+ * o1 [n, heads, head_dim] bf16 (in/out) with its lse1 [heads, ld_lse1] fp32 (in/out), o2 / lse2 [heads, ld_lse2]
+ * the second part; rows [0, n) of each. head_dim a multiple of 32. */
+ORL_API int orl_lse_merge(void* o1, float* lse1, const void* o2, const float* lse2, long long n, long long ld_lse1,
+                  long long ld_lse2, int heads, int head_dim, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ONEREEL_B200_H */

@@ -1,0 +1,201 @@
+"""Varlen attention on the B200 kernel (onereel_b200/csrc/attn_fwd.cu) — the drop-in for src/onereel/attention.py.
+
+Same functions, arguments and return values as the reference module (attention.py:13-84): `cu_seqlens`, `dense`,
+`varlen`, `varlen_lse`, `packed`, `packed_lse`, `overlapping_ranges`, and the module global `BACKEND`. The reference
+selects FlashAttention-2/-3 by BACKEND; here every value runs the sm_100a kernel ('b200'; the reference's 'fa2', 'fa3'
+and 'auto' are accepted so existing callers keep working). There is no CPU or library fallback: inputs must be bf16
+CUDA tensors with head_dim 64 or 128.
+
+Kernel failures: the kernel never hangs; a bounded wait that gives up sets a per-device error word. `check()`
+synchronises and raises if it is set (tests and benchmarks call it; it costs a device sync).
+"""
+from __future__ import annotations
+
+from collections import OrderedDict
+
+import numpy as np
+import torch
+
+from onereel_b200 import _lib as L
+from onereel_b200.pack import pack_rows
+
+BACKEND = 'b200'         # 'b200' (also accepted: the reference's 'fa2' | 'fa3' | 'auto', all served by this kernel)
+_BACKENDS = ('b200', 'fa2', 'fa3', 'auto')
+
+
+def backend() -> str:
+    if BACKEND not in _BACKENDS:
+        raise ImportError(f'unknown attention backend {BACKEND!r}')
+    return 'b200'
+
+
+def cu_seqlens(lengths, device='cuda') -> torch.Tensor:
+    """attention.py:28-29: int32 [0, cumsum(lengths)]"""
+    return torch.tensor([0] + np.cumsum(lengths).tolist(), dtype=torch.int32, device=device)
+
+
+# ------------------------------------------------------------------------------------------------ plans and errors
+
+_PLANS: OrderedDict = OrderedDict()
+_ERR: dict = {}
+
+
+def _err_word(device: torch.device) -> torch.Tensor:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _ERR:
+        _ERR[key] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _ERR[key]
+
+
+def check(device=None) -> None:
+    """synchronise and raise if a kernel on `device` (default: every device used) reported a timeout"""
+    for key, w in list(_ERR.items()):
+        if device is not None and torch.device(device).index not in (None, key):
+            continue
+        bits = int(w.item())
+        if bits:
+            w.zero_()
+            raise L.OrlError(f'attention kernel on cuda:{key} gave up waiting: {L.describe_error_bits(bits)}')
+
+
+def plan(q_start, q_len, k_start, k_len, heads: int, device) -> tuple[torch.Tensor, int]:
+    """device work list for segments given as (start, length) rows (cached: layouts repeat every layer and step)"""
+    key = (tuple(q_start), tuple(q_len), tuple(k_start), tuple(k_len), heads, str(device))
+    hit = _PLANS.get(key)
+    if hit is not None:
+        _PLANS.move_to_end(key)
+        return hit
+    arrs = [np.ascontiguousarray(x, dtype=np.int32) for x in (q_start, q_len, k_start, k_len)]
+    n_seg = len(arrs[0])
+    need = L.lib().orl_attn_plan_ranges(*(L.i32p(a) for a in arrs), n_seg, heads, None, 0)
+    if need >= 0:                                   # nothing to do
+        need_n = 0
+    else:
+        L.check(need if need > -1000 else 0, 'orl_attn_plan_ranges')
+        need_n = -need - 1000
+    work = np.zeros(max(need_n, 1), dtype=L.WORK_DTYPE)
+    n = L.check(L.lib().orl_attn_plan_ranges(*(L.i32p(a) for a in arrs), n_seg, heads, work.ctypes.data, len(work)),
+                'orl_attn_plan_ranges')
+    dev = torch.from_numpy(work.view(np.uint8)).to(device)
+    _PLANS[key] = (dev, n)
+    if len(_PLANS) > 512:
+        _PLANS.popitem(last=False)
+    return dev, n
+
+
+def _host_list(x) -> list[int]:
+    return x.tolist() if isinstance(x, torch.Tensor) else [int(v) for v in x]
+
+
+def _check_inputs(q, k, v):
+    for name, x in (('q', q), ('k', k), ('v', v)):
+        if not (isinstance(x, torch.Tensor) and x.is_cuda and x.dtype == torch.bfloat16):
+            raise TypeError(f'{name} must be a bf16 CUDA tensor (the B200 path has no fallback), got '
+                            f'{getattr(x, "dtype", type(x))} on {getattr(x, "device", "?")}')
+        if x.dim() != 3 or x.stride(-1) != 1 or x.stride(1) != x.shape[2] or x.stride(0) != x.shape[1] * x.shape[2]:
+            raise ValueError(f'{name} must be a contiguous [rows, heads, head_dim] tensor, got {tuple(x.shape)} '
+                             f'strides {x.stride()}')
+    if q.shape[1:] != k.shape[1:] or k.shape != v.shape:
+        raise ValueError(f'shape mismatch q {tuple(q.shape)} k {tuple(k.shape)} v {tuple(v.shape)}')
+    if q.shape[2] not in (64, 128):
+        raise ValueError(f'head_dim {q.shape[2]} not supported (64 or 128)')
+
+
+def attend(q, k, v, q_start, q_len, k_start, k_len, out=None, lse=None, scale=None, stream=None):
+    """the kernel call: segment i = q rows q_start[i] + [0, q_len[i]) attending to k / v rows k_start[i] + [0, k_len[i]).
+    out [Nq, H, D] bf16 (allocated if None); lse None, True (allocate [H, Nq] fp32) or a tensor."""
+    _check_inputs(q, k, v)
+    Nq, H, Dh = q.shape
+    dev = q.device
+    work, n = plan(q_start, q_len, k_start, k_len, H, dev)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is True:
+        lse = torch.empty(H, Nq, dtype=torch.float32, device=dev)
+    scale = Dh ** -0.5 if scale is None else float(scale)
+    s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    L.check(L.lib().orl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                 None if lse is None else lse.data_ptr(), Nq, k.shape[0], H, Dh, scale,
+                                 work.data_ptr(), n, _err_word(dev).data_ptr(), s), 'orl_attn_fwd')
+    return out, lse
+
+
+def _cu_to_ranges(cu_q, cu_k):
+    cq, ck = _host_list(cu_q), _host_list(cu_k)
+    if len(cq) != len(ck):
+        raise ValueError('cu_seqlens_q and cu_seqlens_k differ in length')
+    qs, ks = cq[:-1], ck[:-1]
+    ql = [b - a for a, b in zip(cq[:-1], cq[1:])]
+    kl = [b - a for a, b in zip(ck[:-1], ck[1:])]
+    if any(x < 0 for x in ql + kl):
+        raise ValueError('cu_seqlens must be non-decreasing')
+    return qs, ql, ks, kl
+
+
+def varlen(q, k, v, cu_q, cu_k, max_q, max_k):
+    """attention.py:39-43: packed q [Nq, H, D], k / v [Nk, H, D] -> out [Nq, H, D]"""
+    return attend(q, k, v, *_cu_to_ranges(cu_q, cu_k))[0]
+
+
+def varlen_lse(q, k, v, cu_q, cu_k, max_q, max_k):
+    """attention.py:46-53: (out [Nq, H, D], lse [H, Nq] fp32, natural log)"""
+    return attend(q, k, v, *_cu_to_ranges(cu_q, cu_k), lse=True)
+
+
+def _pack_segments(segments):
+    lq = [s[0].shape[0] for s in segments]
+    lk = [s[1].shape[0] for s in segments]
+    q0 = segments[0][0]
+    H, Dh = q0.shape[1:]
+    qp = q0.new_empty(sum(lq), H, Dh)
+    kp = q0.new_empty(sum(lk), H, Dh)
+    vp = q0.new_empty(sum(lk), H, Dh)
+    c = lambda x: x if x.is_contiguous() else x.contiguous()
+    pack_rows([c(s[0]) for s in segments], qp)
+    pack_rows([c(s[1]) for s in segments], kp)
+    pack_rows([c(s[2]) for s in segments], vp)
+    cq, ck = np.cumsum([0] + lq), np.cumsum([0] + lk)
+    return qp, kp, vp, lq, list(cq[:-1]), lk, list(ck[:-1])
+
+
+def packed_lse(segments):
+    """attention.py:56-62: list of (out, lse [H, n]) per segment, one kernel call"""
+    qp, kp, vp, lq, qs, lk, ks = _pack_segments(segments)
+    o, lse = attend(qp, kp, vp, qs, lq, ks, lk, lse=True)
+    return list(zip(o.split(lq), lse.split(lq, dim=1)))
+
+
+def packed(segments):
+    """attention.py:65-71: segments = list of (q, k, v) -> list of outputs, one gather/pack launch per tensor and one
+    attention launch"""
+    qp, kp, vp, lq, qs, lk, ks = _pack_segments(segments)
+    return attend(qp, kp, vp, qs, lq, ks, lk)[0].split(lq)
+
+
+def overlapping_ranges(q, k, v, q_ranges, k_ranges):
+    """attention.py:74-84: q rows q_ranges[j] attend to k / v rows k_ranges[j], read in place (no copy); q_ranges
+    tile q in order"""
+    qs = [a for a, _ in q_ranges]
+    ql = [b - a for a, b in q_ranges]
+    if qs and (qs[0] != 0 or any(qs[i] + ql[i] != qs[i + 1] for i in range(len(qs) - 1)) or qs[-1] + ql[-1] != q.shape[0]):
+        raise ValueError('q_ranges must tile q in order')
+    return attend(q, k, v, qs, ql, [a for a, _ in k_ranges], [b - a for a, b in k_ranges])[0]
+
+
+def dense(q, k, v):
+    """attention.py:32-36: q, k, v [B, S, H, D] -> [B, S, H, D], full attention per batch entry"""
+    B, S, H, Dh = q.shape
+    Sk = k.shape[1]
+    c = lambda x: x.reshape(B * x.shape[1], H, Dh).contiguous()
+    o = attend(c(q), c(k), c(v), [b * S for b in range(B)], [S] * B, [b * Sk for b in range(B)], [Sk] * B)[0]
+    return o.view(B, S, H, Dh)
+
+
+def lse_merge(o1, lse1, o2, lse2):
+    """in place: (o1, lse1) <- the merge of two partial results over disjoint keys (hunyuan15.py:274-276,
+    ring.py:63-70). o [n, H, D] bf16 contiguous, lse [H, >= n] fp32 (row stride = its second dimension)."""
+    n, H, Dh = o1.shape
+    s = torch.cuda.current_stream(o1.device).cuda_stream
+    L.check(L.lib().orl_lse_merge(o1.data_ptr(), lse1.data_ptr(), o2.data_ptr(), lse2.data_ptr(), n, lse1.stride(0),
+                                  lse2.stride(0), H, Dh, s), 'orl_lse_merge')
+    return o1, lse1

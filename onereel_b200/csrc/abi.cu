@@ -1,0 +1,37 @@
+// Library-wide C entry points: version and error strings.
+#include <cstdio>
+#include <cstring>
+
+#include "orl_common.h"
+#include "ptx.cuh"
+
+extern "C" const char* orl_version(void) { return "onereel_b200 0.1.0 (sm_100a)"; }
+
+extern "C" const char* orl_error_string(int code) {
+  switch (code) {
+    case ORL_OK: return "ok";
+    case ORL_ERR_ARG: return "invalid argument";
+    case ORL_ERR_ALIGN: return "pointer, offset or size not 16-byte aligned";
+    case ORL_ERR_UNSUPPORTED: return "unsupported head_dim (64 or 128)";
+    case ORL_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable from the driver";
+    case ORL_ERR_TENSOR_MAP: return "the driver rejected a TMA tensor map";
+    case ORL_ERR_LAUNCH: return "kernel launch failed";
+    case ORL_ERR_CAPACITY: return "caller buffer too small";
+    default: return "unknown error";
+  }
+}
+
+extern "C" int orl_error_bits_describe(int bits, char* buf, int cap) {
+  if (buf == nullptr || cap <= 0) return ORL_ERR_ARG;
+  buf[0] = 0;
+  const struct { int bit; const char* what; } names[] = {
+      {orl::kErrTimeoutLoad, "producer timed out waiting for a free K/V stage"},
+      {orl::kErrTimeoutMma, "MMA warp timed out waiting for a tile or for P"},
+      {orl::kErrTimeoutSoftmax, "softmax warps timed out waiting for S or O"},
+      {orl::kErrTimeoutDrain, "wind-down timed out waiting for in-flight copies"},
+  };
+  int n = 0;
+  for (const auto& e : names)
+    if (bits & e.bit) n += snprintf(buf + n, n < cap ? cap - n : 0, "%s%s", n ? "; " : "", e.what);
+  return ORL_OK;
+}

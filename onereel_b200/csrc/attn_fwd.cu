@@ -1,0 +1,476 @@
+// Packed variable-length scene attention, forward, bf16 in / fp32 accumulate / bf16 out, for sm_100a.
+//
+// Replaces the FlashAttention varlen call of the reference (src/onereel/attention.py:39-53 `varlen` / `varlen_lse`,
+// reached from `packed` / `packed_lse` at 56-71): for every segment i, rows cu_q[i]..cu_q[i+1] of q attend to rows
+// cu_k[i]..cu_k[i+1] of k / v, non-causal, softmax scale `scale` (D^-0.5 by default), optional natural-log LSE [H, Nq].
+//
+// One CTA computes one work item = (segment, head, up to 256 query rows as two 128-row tiles):
+//   warp 0      TMA producer: Q tiles once, then K_j / V_j tiles of 128 rows into a ring of shared-memory stages
+//   warp 1      TMEM owner and MMA issuer (one elected thread): S_t = Q_t K_j^T (SS form), O_t += P_t V_j (TS form,
+//               P read from TMEM), each group committed to an mbarrier
+//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: thread = query row = TMEM lane. Loads the S row,
+//               online max / exp2 / sum, writes P (bf16) over its S columns, rescales its O row in TMEM only when
+//               the running max grows by more than 2^8 (otherwise keeps the stale max: the result is identical and
+//               P stays <= 256), then normalises O and stores the bf16 row and its LSE.
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D,256+2D).
+// Every mbarrier wait is bounded (ptx.cuh kWaitLimitNs): a stuck pipeline sets the error word and winds down.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "orl_common.h"
+#include "ptx.cuh"
+
+namespace orl {
+
+template <int D>
+struct AttnCfg {
+  static constexpr int kChunks = D / 64;              // 128-byte swizzle columns per row
+  static constexpr int kTileBytes = 128 * D * 2;      // one 128-row bf16 tile
+  static constexpr int kChunkBytes = 128 * 128;       // one 128-row x 64-column chunk
+  static constexpr int kStages = (D == 128) ? 2 : 4;  // K/V ring depth
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = 2 * kTileBytes;
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_full, drain
+  static constexpr int kBarQ = 0;
+  static constexpr int kBarK = 1;
+  static constexpr int kBarV = kBarK + kStages;
+  static constexpr int kBarE = kBarV + kStages;
+  static constexpr int kBarS = kBarE + kStages;
+  static constexpr int kBarP = kBarS + 2;
+  static constexpr int kBarO = kBarP + 2;
+  static constexpr int kBarDrain = kBarO + 1;
+  static constexpr int kNumBars = kBarDrain + 1;
+  static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  // TMEM column of S_t / O_t (t = 0, 1)
+  __host__ __device__ static constexpr uint32_t col_s(int t) { return t ? 128u : 0u; }
+  __host__ __device__ static constexpr uint32_t col_o(int t) { return t ? 256u + D : 256u; }
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+constexpr int kThreads = 384;
+
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* err) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(err, kErrTimeoutDrain);
+      return;
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const AttnWork* __restrict__ work,
+                    __nv_bfloat16* __restrict__ out, float* __restrict__ lse, long long nq_total, int heads,
+                    float scale_log2, int* __restrict__ err) {
+  using C = AttnCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOff + C::kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) -> uint32_t { return sbase + C::kBarOff + 8u * i; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const AttnWork wi = work[blockIdx.x];
+  const int n_qt = wi.q_len > 128 ? 2 : 1;
+  const int n_kv = (wi.k_len + 127) >> 7;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(C::kBarQ), 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar(C::kBarK + s), 1);
+      mbar_init(bar(C::kBarV + s), 1);
+      mbar_init(bar(C::kBarE + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(C::kBarS + t), 1);
+      mbar_init(bar(C::kBarP + t), 128);
+    }
+    mbar_init(bar(C::kBarO), 1);
+    mbar_init(bar(C::kBarDrain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (elect_one() && n_kv > 0) {
+      tma_prefetch_map(&tm_q);
+      tma_prefetch_map(&tm_k);
+      tma_prefetch_map(&tm_v);
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();
+      const int x0 = wi.head * D;
+      mbar_expect_tx(bar(C::kBarQ), n_qt * C::kTileBytes);
+      for (int t = 0; t < n_qt; ++t)
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_2d(sbase + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, &tm_q, bar(C::kBarQ), x0 + 64 * c,
+                      wi.q_row0 + 128 * t, pol_q);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % C::kStages;
+        if (j >= C::kStages && !mbar_wait(bar(C::kBarE + s), ((j / C::kStages) - 1) & 1, abort_flag)) {
+          atomicOr(err, kErrTimeoutLoad);
+          break;
+        }
+        const int y = wi.k_row0 + 128 * j;
+        mbar_expect_tx(bar(C::kBarK + s), C::kTileBytes);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_2d(sbase + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, &tm_k, bar(C::kBarK + s),
+                      x0 + 64 * c, y, pol_kv);
+        mbar_expect_tx(bar(C::kBarV + s), C::kTileBytes);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_2d(sbase + C::kVOff + s * C::kTileBytes + c * C::kChunkBytes, &tm_v, bar(C::kBarV + s),
+                      x0 + 64 * c, y, pol_kv);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // wind down: every copy this thread started must land before the CTA's shared memory is released
+        drain_wait(bar(C::kBarQ), 0, err);
+        for (int j = std::max(0, issued - C::kStages); j < issued; ++j) {
+          const int s = j % C::kStages;
+          drain_wait(bar(C::kBarK + s), (j / C::kStages) & 1, err);
+          drain_wait(bar(C::kBarV + s), (j / C::kStages) & 1, err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one() && n_kv > 0) {
+      constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
+      constexpr uint32_t kIdescO = idesc_bf16(128, D, false, true);
+      bool ok = mbar_wait(bar(C::kBarQ), 0, abort_flag);
+      auto issue_s = [&](int t, int s) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::kChunkBytes + (kk & 3) * 32;
+          const uint64_t a = smem_desc_sw128(sbase + C::kQOff + t * C::kTileBytes + off, 16, 1024);
+          const uint64_t b = smem_desc_sw128(sbase + C::kKOff + s * C::kTileBytes + off, 16, 1024);
+          mma_ss(tmem + C::col_s(t), a, b, kIdescS, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_o = [&](int t, int s, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t b = smem_desc_sw128(sbase + C::kVOff + s * C::kTileBytes + kk * 2048, C::kChunkBytes, 1024);
+          mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, b, kIdescO, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      if (ok) ok = mbar_wait(bar(C::kBarK + 0), 0, abort_flag);
+      if (ok) {
+        issue_s(0, 0);
+        mma_commit(bar(C::kBarS + 0));
+        if (n_qt == 2) {
+          issue_s(1, 0);
+          mma_commit(bar(C::kBarS + 1));
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % C::kStages;
+        const int s2 = (j + 1) % C::kStages;
+        const bool more = j + 1 < n_kv;
+        ok = mbar_wait(bar(C::kBarV + s), (j / C::kStages) & 1, abort_flag) &&
+             mbar_wait(bar(C::kBarP + 0), j & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        issue_o(0, s, j > 0);
+        if (more) {
+          ok = mbar_wait(bar(C::kBarK + s2), ((j + 1) / C::kStages) & 1, abort_flag);
+          if (!ok) break;
+          issue_s(0, s2);
+          mma_commit(bar(C::kBarS + 0));
+        }
+        if (n_qt == 2) {
+          ok = mbar_wait(bar(C::kBarP + 1), j & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_o(1, s, j > 0);
+        }
+        mma_commit(bar(C::kBarE + s));
+        if (n_qt == 2 && more) {
+          issue_s(1, s2);
+          mma_commit(bar(C::kBarS + 1));
+        }
+      }
+      if (ok) {
+        mma_commit(bar(C::kBarO));
+      } else {
+        atomicOr(err, kErrTimeoutMma);
+        mma_commit(bar(C::kBarDrain));
+        drain_wait(bar(C::kBarDrain), 0, err);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax / correction / epilogue
+    const int t = (warp - 4) >> 2;
+    const int quad = warp & 3;
+    const int row = 32 * quad + lane;                 // row within tile t = TMEM lane
+    const int item_row = 128 * t + row;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
+    const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
+    const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
+    const bool row_valid = item_row < wi.q_len;
+    __nv_bfloat16* orow = out + (static_cast<long long>(wi.q_row0) + item_row) * heads * D + wi.head * D;
+    if (t < n_qt) {
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = n_kv > 0;
+      for (int j = 0; ok && j < n_kv; ++j) {
+        ok = mbar_wait(bar(C::kBarS + t), j & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t r[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, r[c]);
+        tmem_wait_ld();
+        const int valid = wi.k_len - 128 * j;
+        if (valid < 128) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * c + i >= valid) r[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = __uint_as_float(r[0][0]), mx1 = __uint_as_float(r[1][0]);
+        float mx2 = __uint_as_float(r[2][0]), mx3 = __uint_as_float(r[3][0]);
+#pragma unroll
+        for (int i = 1; i < 32; ++i) {
+          mx0 = fmaxf(mx0, __uint_as_float(r[0][i]));
+          mx1 = fmaxf(mx1, __uint_as_float(r[1][i]));
+          mx2 = fmaxf(mx2, __uint_as_float(r[2][i]));
+          mx3 = fmaxf(mx3, __uint_as_float(r[3][i]));
+        }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float m_new = fmaxf(m_run, mx);
+        const bool need = (m_new - m_run) * scale_log2 > 8.0f;
+        const float m_use = need ? m_new : m_run;
+        const float alpha = ex2((m_run - m_use) * scale_log2);
+        const float neg = -m_use * scale_log2;
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t p[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = 2 * h + (i >> 4);
+            const int e = (2 * i) & 31;
+            const float p0 = ex2(fmaf(__uint_as_float(r[c][e]), scale_log2, neg));
+            const float p1 = ex2(fmaf(__uint_as_float(r[c][e + 1]), scale_log2, neg));
+            sum0 += p0;
+            sum1 += p1;
+            p[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st32(s_addr + 32 * h, p);
+        }
+        l_run = l_run * alpha + (sum0 + sum1);
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + 32 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_addr + 32 * c, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(C::kBarP + t));
+        m_run = m_use;
+      }
+      if (ok) ok = mbar_wait(bar(C::kBarO), 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        const float inv = 1.0f / l_run;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+          if (row_valid) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+              dst[v] = w;
+            }
+          }
+        }
+        if (lse != nullptr && row_valid)
+          lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] =
+              (m_run * scale_log2 + lg2(l_run)) * 0.69314718055994530942f;
+      } else if (n_kv > 0) {
+        atomicOr(err, kErrTimeoutSoftmax);
+      } else if (row_valid) {
+        // a segment without keys: zero output, LSE -inf
+        uint4* dst = reinterpret_cast<uint4*>(orow);
+        for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+        if (lse != nullptr) lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] = -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host side
+
+// cuTensorMapEncodeTiled (driver API, cuda.h), fetched through the runtime so the library needs no -lcuda.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 map over rows x (heads * D) with 128-row x 64-column boxes, 128-byte swizzle, zero fill out of bounds.
+static int make_rows_map(CUtensorMap* map, const void* base, long long rows, int row_elems) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return ORL_ERR_DRIVER;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_elems), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_elems) * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ORL_OK : ORL_ERR_TENSOR_MAP;
+}
+
+template <int D>
+static int launch_attn(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
+                       long long nk, int heads, float scale, const AttnWork* work, int n_items, int* err,
+                       cudaStream_t stream) {
+  using C = AttnCfg<D>;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_rows_map(&mq, q, nq, heads * D)) != ORL_OK) return rc;
+  if ((rc = make_rows_map(&mk, k, nk, heads * D)) != ORL_OK) return rc;
+  if ((rc = make_rows_map(&mv, v, nk, heads * D)) != ORL_OK) return rc;
+  static std::once_flag once;
+  static cudaError_t attr_rc = cudaSuccess;
+  std::call_once(once, [] {
+    attr_rc = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  });
+  if (attr_rc != cudaSuccess) return ORL_ERR_LAUNCH;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  attn_fwd_kernel<D><<<n_items, kThreads, C::kSmemBytes, stream>>>(
+      mq, mk, mv, work, static_cast<__nv_bfloat16*>(out), lse, nq, heads, scale_log2, err);
+  return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
+}
+
+}  // namespace orl
+
+using namespace orl;
+
+extern "C" int orl_attn_plan_ranges(const int32_t* q_start, const int32_t* q_len, const int32_t* k_start,
+                                    const int32_t* k_len, int n_seg, int heads, AttnWork* work, int capacity) {
+  if (q_start == nullptr || q_len == nullptr || k_start == nullptr || k_len == nullptr || n_seg < 0 || heads <= 0)
+    return ORL_ERR_ARG;
+  std::vector<int> order;
+  long long need = 0;
+  for (int i = 0; i < n_seg; ++i) {
+    if (q_len[i] < 0 || k_len[i] < 0 || q_start[i] < 0 || k_start[i] < 0) return ORL_ERR_ARG;
+    if (q_len[i] == 0) continue;
+    order.push_back(i);
+    need += static_cast<long long>(heads) * ((q_len[i] + 255) / 256);
+  }
+  if (need > 0x3fffffff) return ORL_ERR_ARG;
+  if (work == nullptr || capacity < need) return -static_cast<int>(need) - 1000;   // caller sizes the buffer
+  // longest key range first (largest items first), items of one (segment, head) adjacent so their K/V share L2
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return k_len[a] > k_len[b]; });
+  int n = 0;
+  for (int i : order)
+    for (int h = 0; h < heads; ++h)
+      for (int p = 0; p < q_len[i]; p += 256) {
+        AttnWork w;
+        w.q_row0 = q_start[i] + p;
+        w.q_len = std::min(256, q_len[i] - p);
+        w.k_row0 = k_start[i];
+        w.k_len = k_len[i];
+        w.head = h;
+        w.seg = i;
+        w.pad0 = w.pad1 = 0;
+        work[n++] = w;
+      }
+  return n;
+}
+
+extern "C" int orl_attn_plan(const int32_t* cu_q, const int32_t* cu_k, int n_seg, int heads, AttnWork* work,
+                             int capacity) {
+  if (cu_q == nullptr || cu_k == nullptr || n_seg < 0) return ORL_ERR_ARG;
+  std::vector<int32_t> qs(n_seg), ql(n_seg), ks(n_seg), kl(n_seg);
+  for (int i = 0; i < n_seg; ++i) {
+    qs[i] = cu_q[i];
+    ql[i] = cu_q[i + 1] - cu_q[i];
+    ks[i] = cu_k[i];
+    kl[i] = cu_k[i + 1] - cu_k[i];
+  }
+  return orl_attn_plan_ranges(qs.data(), ql.data(), ks.data(), kl.data(), n_seg, heads, work, capacity);
+}
+
+extern "C" int orl_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
+                            long long nk, int heads, int head_dim, float scale, const AttnWork* work_dev,
+                            int n_items, int* err_dev, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || work_dev == nullptr || err_dev == nullptr)
+    return ORL_ERR_ARG;
+  if (nq < 0 || nk < 0 || heads <= 0 || n_items < 0 || !(scale > 0.f)) return ORL_ERR_ARG;
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+        reinterpret_cast<uintptr_t>(out)) & 15u) != 0)
+    return ORL_ERR_ALIGN;
+  if (n_items == 0 || nq == 0) return ORL_OK;
+  if (nk == 0) {   // every item has k_len 0 and loads nothing; the K/V maps only need a valid address
+    k = v = q;
+    nk = nq;
+  }
+  switch (head_dim) {
+    case 64:
+      return launch_attn<64>(q, k, v, out, lse, nq, nk, heads, scale, work_dev, n_items, err_dev, stream);
+    case 128:
+      return launch_attn<128>(q, k, v, out, lse, nq, nk, heads, scale, work_dev, n_items, err_dev, stream);
+    default:
+      return ORL_ERR_UNSUPPORTED;
+  }
+}

@@ -1,0 +1,184 @@
+"""Scene-scope layout builder: a scene layout -> packed segments -> gather/pack run tables + attention work list.
+
+This is the B200 replacement of the reference's per-layer Python segment assembly
+(src/onereel/models/hunyuan15.py:153-170 `_segments`, 212-251 `Processor.scene`, 279-303 `Processor.ulysses`;
+src/onereel/models/wan.py:110-152 `ranges` / `scene`; src/onereel/attention.py:56-71 `packed`). The reference builds
+the segment list with Python loops and torch.cat copies in every layer; here the list is compiled once per layout
+(cached: layouts change at most once per denoising step) into
+
+  - a K/V run table: per segment, its key rows as row runs from the sources (this rank's video rows, the received
+    exchange buffers, the text rows), executed by the pack kernel for K and V in one launch (two planes);
+  - the query rows read in place: video queries straight from the rank's q, text queries from eq — no q pack;
+  - an output scatter run table (packed text outputs -> their rows of ot; video outputs are written in place);
+  - the attention work list and cu_seqlens (bit-exact with attention.cu_seqlens of the reference's call).
+
+Packed segment order (must match the reference, pinned by tests/golden/segments.json): per scene piece j ascending,
+the video segment (queries = its token rows; keys = key_frames(j) tokens, then sentence j's text rows), then, if the
+rank runs scene j's text queries, the text segment (queries = sentence j; keys = scene j's own frames, then sentence j).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from onereel_b200 import attention as A
+from onereel_b200.pack import RunTable
+
+# source ids of row runs
+VIDEO, TEXT, REMOTE = 0, 1, 2
+
+
+def frame_runs(frames) -> list[tuple[int, int]]:
+    """frame list in order -> contiguous frame runs (comm.py:115-123 `runs`)"""
+    out = []
+    for f in frames:
+        if out and out[-1][1] == f:
+            out[-1][1] = f + 1
+        else:
+            out.append([f, f + 1])
+    return [(a, b) for a, b in out]
+
+
+def frame_tokens(frames, T: int) -> list[tuple[int, int]]:
+    """frame list -> token intervals in the list's order (comm.py:84-85)"""
+    return [(a * T, b * T) for a, b in frame_runs(frames)]
+
+
+@dataclass
+class Segment:
+    kind: str                      # 'v' video queries, 't' text queries
+    scene: int
+    q: tuple                       # (source, row lo, row hi) in source rows (VIDEO rows are rank-local)
+    kv: list                       # [(source, row lo, row hi)] in key order
+    out: tuple                     # where the output rows go: ('v', local lo, hi) or ('t', text lo, hi)
+
+    @property
+    def lq(self) -> int:
+        return self.q[2] - self.q[1]
+
+    @property
+    def lk(self) -> int:
+        return sum(hi - lo for _, lo, hi in self.kv)
+
+
+def text_ranges(counts) -> list[tuple[int, int]]:
+    """hunyuan15.py:87-89"""
+    c = np.cumsum([0] + list(counts))
+    return [(int(c[j]), int(c[j + 1])) for j in range(len(counts))]
+
+
+def video_key_runs(frames, T, own, remote_index):
+    """token intervals of a frame list -> source runs: rows inside own = (a, b) come from the local rows, the others
+    from the received buffer intervals (remote_index: sorted [(token lo, token hi, buffer row of lo)])"""
+    a, b = own
+    runs = []
+    for lo, hi in frame_tokens(frames, T):
+        while lo < hi:
+            if a <= lo < b:
+                e = min(hi, b)
+                runs.append((VIDEO, lo - a, e - a))
+            else:
+                hit = next(((x, y, r) for x, y, r in remote_index if x <= lo < y), None)
+                if hit is None:
+                    raise ValueError(f'token {lo} is neither local ({a}, {b}) nor received')
+                x, y, r = hit
+                e = min(hi, y)
+                runs.append((REMOTE, r + lo - x, r + e - x))
+            lo = e
+    return _merge_runs(runs)
+
+
+def _merge_runs(runs):
+    out = []
+    for s, lo, hi in runs:
+        if hi <= lo:
+            continue
+        if out and out[-1][0] == s and out[-1][2] == lo:
+            out[-1] = (s, out[-1][1], hi)
+        else:
+            out.append((s, lo, hi))
+    return out
+
+
+def scene_segments(layout, T, counts, scenes, text_for, own, remote_index=()):
+    """the packed segments of `scenes` [(j, (token lo, token hi))] on a rank owning video tokens own = (a, b);
+    text_for: scenes whose text queries this call runs (hunyuan15.py:153-170)"""
+    tr = text_ranges(counts) if counts is not None else None
+    a = own[0]
+    segs = []
+    for j, (qlo, qhi) in scenes:
+        kv = video_key_runs(layout.key_frames(j), T, own, remote_index)
+        if tr is not None and tr[j][1] > tr[j][0]:
+            kv = kv + [(TEXT, tr[j][0], tr[j][1])]
+        segs.append(Segment('v', j, (VIDEO, qlo - a, qhi - a), kv, ('v', qlo - a, qhi - a)))
+        if tr is not None and j in text_for:
+            t0, t1 = tr[j]
+            kv_t = video_key_runs(layout.frames[j], T, own, remote_index) + [(TEXT, t0, t1)]
+            segs.append(Segment('t', j, (TEXT, t0, t1), kv_t, ('t', t0, t1)))
+    return segs
+
+
+@dataclass
+class ScenePlan:
+    """compiled segments of one packed call on one device: K/V run table (slots VIDEO, TEXT, REMOTE -> slot 3 =
+    packed buffer), query rows in place per segment, the attention work list, cu_seqlens"""
+    segs: list
+    row_bytes: int
+    heads: int
+    device: torch.device
+    kv_table: RunTable = None
+    n_keys: int = 0
+    lq: list = field(default_factory=list)
+    lk: list = field(default_factory=list)
+    cu_q: list = field(default_factory=list)
+    cu_k: list = field(default_factory=list)
+
+    def __post_init__(self):
+        rb = self.row_bytes
+        src_slot, dst_slot, src_off, dst_off, nbytes = [], [], [], [], []
+        row = 0
+        for s in self.segs:
+            for src, lo, hi in s.kv:
+                src_slot.append(src)
+                dst_slot.append(3)
+                src_off.append(lo * rb)
+                dst_off.append(row * rb)
+                nbytes.append((hi - lo) * rb)
+                row += hi - lo
+        self.n_keys = row
+        self.kv_table = RunTable(src_slot, dst_slot, src_off, dst_off, nbytes, self.device)
+        self.lq = [s.lq for s in self.segs]
+        self.lk = [s.lk for s in self.segs]
+        self.cu_q = np.concatenate([[0], np.cumsum(self.lq)]).astype(np.int32).tolist()
+        self.cu_k = np.concatenate([[0], np.cumsum(self.lk)]).astype(np.int32).tolist()
+
+    def pack_kv(self, k_video, v_video, k_text, v_text, k_remote=None, v_remote=None, out=None):
+        """one pack launch for K and V (two planes): returns packed (k, v) [n_keys, H, D]"""
+        H, Dh = k_video.shape[1:]
+        if out is None:
+            kp = k_video.new_empty(self.n_keys, H, Dh)
+            vp = k_video.new_empty(self.n_keys, H, Dh)
+        else:
+            kp, vp = out
+        ptr = lambda x: 0 if x is None else x.data_ptr()
+        src = [ptr(k_video), ptr(k_text), ptr(k_remote), 0, ptr(v_video), ptr(v_text), ptr(v_remote), 0]
+        dst = [0, 0, 0, kp.data_ptr(), 0, 0, 0, vp.data_ptr()]
+        self.kv_table.run(src, dst, n_planes=2)
+        return kp, vp
+
+
+def attend_segments(plan: ScenePlan, q, eq, kp, vp, ov, ot, lse_v=None, lse_t=None):
+    """attention of every segment of the plan: queries read in place from q (video) and eq (text). Video outputs go
+    straight to their rows of ov; text outputs are computed into their rows of ot. One kernel launch per query
+    source (video, text)."""
+    for kind, qsrc, dst, lse in (('v', q, ov, lse_v), ('t', eq, ot, lse_t)):
+        idx = [i for i, s in enumerate(plan.segs) if s.kind == kind]
+        if not idx:
+            continue
+        qs = [plan.segs[i].q[1] for i in idx]
+        ql = [plan.segs[i].lq for i in idx]
+        ks = [plan.cu_k[i] for i in idx]
+        kl = [plan.lk[i] for i in idx]
+        A.attend(qsrc, kp, vp, qs, ql, ks, kl, out=dst, lse=lse)
