@@ -28,13 +28,16 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 CFG2 = dict(lengths=[8, 6, 10, 7], T=1590, text=128, heads=16, dim=128, memory=[0, 8, 14, 24])
+# a reduced cfg2 (first two scenes) for profiler captures: inputs still larger than L2, a few hundred MB on the device
+SMALL = dict(lengths=[8, 6], T=1590, text=128, heads=16, dim=128, memory=[0, 8])
 METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
 
 
-def cfg2_layout():
+def cfg_layout(cfg):
+    """frame memory = the first latent frame of the first scenes (BASELINE cfg1's rule), read by every other scene"""
     from onereel_b200.layout import SceneLayout
-    lay = SceneLayout(CFG2['lengths'], halo=0)
-    lay.extra = {j: [f for f in CFG2['memory'] if not lo <= f < hi] for j, (lo, hi) in enumerate(lay.ranges)}
+    lay = SceneLayout(cfg['lengths'], halo=0)
+    lay.extra = {j: [f for f in cfg['memory'] if not lo <= f < hi] for j, (lo, hi) in enumerate(lay.ranges)}
     return lay
 
 
@@ -142,10 +145,12 @@ def make_inputs(lay, T, counts, H, Dh, dev, seed=0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small'],
+                    help='small: the first two scenes of cfg2, for profiler captures (not a bench line)')
     args = ap.parse_args()
     if args.impl == 'reference':
         return run_reference(args)
@@ -162,9 +167,10 @@ def main():
         from datetime import timedelta
         dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
 
-    lay = cfg2_layout()
-    T, H, Dh = CFG2['T'], CFG2['heads'], CFG2['dim']
-    counts = [CFG2['text']] * lay.n_scenes
+    cfg = CFG2 if args.workload == 'cfg2' else SMALL
+    lay = cfg_layout(cfg)
+    T, H, Dh = cfg['T'], cfg['heads'], cfg['dim']
+    counts = [cfg['text']] * lay.n_scenes
     L = lay.n_frames * T
     q, k, v, eq, ek, ev = make_inputs(lay, T, counts, H, Dh, dev, seed=rank)
     mine = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
@@ -253,15 +259,16 @@ def main():
     peak_burst, peak_sus, hbm, peak_kind = peaks()
     achieved = flops / (attn_ms * 1e-3) / 1e12
     cb = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and args.workload == 'cfg2':
         cb, _ = cpu_baseline()
     h2d = sum(x.numel() * x.element_size() for x in host_in)
     d2h = sum(x.numel() * x.element_size() for x in host_out)
     line = dict(metric=METRIC, value=world * flops / (ms * 1e-3) / 1e12, unit='TFLOP/s', n_gpus=world,
                 steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling='weak',
                 vs_baseline=None, dtype='bf16', data='synthetic (seeded; Q/K RMS-normed N(0,1), V N(0,1))',
-                config=dict(workload='cfg2: one HunyuanVideo-1.5-shaped scene-attention layer (pack K/V + attention)',
-                            layout=CFG2, segments=len(plan.segs), sum_q=sum(plan.lq), sum_k=sum(plan.lk),
+                config=dict(workload=f'{args.workload}: one HunyuanVideo-1.5-shaped scene-attention layer '
+                                     '(pack K/V + attention)',
+                            layout=cfg, segments=len(plan.segs), sum_q=sum(plan.lq), sum_k=sum(plan.lk),
                             useful_tflop_per_step=flops / 1e12, parallelism=f'replicas x{world}' if world > 1 else 'single',
                             l2='inputs larger than L2 (q/k/v 203 MB each, packed K/V 486 MB each)'),
                 e2e=dict(value=world * flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s', ms_per_step=e2e_ms,

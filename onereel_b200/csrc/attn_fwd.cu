@@ -474,3 +474,125 @@ extern "C" int orl_attn_fwd(const void* q, const void* k, const void* v, void* o
       return ORL_ERR_UNSUPPORTED;
   }
 }
+
+// ------------------------------------------------------------------------------------------------ allocation-free
+// orl_attn_fwd_noalloc serves callers that cannot call cudaMalloc at all — code running where the CUDA allocator
+// is off limits (inside another framework's memory pool or a custom allocator hook, in a plugin host that owns
+// device memory, or in a process whose allocations are accounted elsewhere) and therefore cannot provide the work
+// list and error word that orl_attn_fwd takes as caller scratch. This variant keeps that scratch in the file-scope
+// array below instead: every GPU that loads the library holds it (kNoAllocScratchBytes, about 512 KiB) until the
+// process exits. Its limits: at most kNoAllocMaxSegments segments and kNoAllocMaxItems work items (one item = one
+// head x up to 256 query rows of one segment); larger calls are rejected with ORL_ERR_CAPACITY before any work.
+// Every call shares the array and it keeps the last call's contents: the error word is cleared at the start of each
+// call. Calls whose kernels overlap on one GPU (issued on two streams, or from two host threads) race on the array,
+// so callers serialise their calls per device; calls on different GPUs do not interact (each GPU has its own copy).
+// The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device current)
+// and caches it; make that first call before any stream capture.
+namespace orl {
+
+constexpr int kNoAllocMaxItems = 16384;
+constexpr int kNoAllocMaxSegments = 4096;
+constexpr int kNoAllocHeaderBytes = 256;   // error word at offset 0, work items from offset 256
+constexpr int kNoAllocScratchBytes = kNoAllocHeaderBytes + kNoAllocMaxItems * static_cast<int>(sizeof(AttnWork));
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mutex;
+static unsigned char* g_noalloc_dev[kNoAllocMaxDevices];        // device address of the array, per device ordinal
+static AttnWork g_noalloc_items[kNoAllocMaxItems];              // host staging of the work list (static, no heap)
+static int32_t g_noalloc_order[kNoAllocMaxSegments];
+
+}  // namespace orl
+
+extern "C" int orl_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
+                                    long long nk, int heads, int head_dim, float scale, const int32_t* cu_q_host,
+                                    const int32_t* cu_k_host, int n_seg, int* status_host, void* stream_ptr) {
+  using namespace orl;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || cu_q_host == nullptr || cu_k_host == nullptr)
+    return ORL_ERR_ARG;
+  if (nq < 0 || nk < 0 || heads <= 0 || n_seg < 0 || !(scale > 0.f)) return ORL_ERR_ARG;
+  if (head_dim != 64 && head_dim != 128) return ORL_ERR_UNSUPPORTED;
+  if (n_seg > kNoAllocMaxSegments) return ORL_ERR_CAPACITY;
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+        reinterpret_cast<uintptr_t>(out)) & 15u) != 0)
+    return ORL_ERR_ALIGN;
+  // validate the segments and count the work items before touching any device state
+  long long items = 0;
+  if (cu_q_host[0] < 0 || cu_k_host[0] < 0) return ORL_ERR_ARG;
+  for (int i = 0; i < n_seg; ++i) {
+    const long long lq = static_cast<long long>(cu_q_host[i + 1]) - cu_q_host[i];
+    const long long lk = static_cast<long long>(cu_k_host[i + 1]) - cu_k_host[i];
+    if (lq < 0 || lk < 0) return ORL_ERR_ARG;
+    items += static_cast<long long>(heads) * ((lq + 255) / 256);
+  }
+  if (n_seg > 0 && (cu_q_host[n_seg] > nq || cu_k_host[n_seg] > nk)) return ORL_ERR_ARG;
+  if (items > kNoAllocMaxItems) return ORL_ERR_CAPACITY;
+
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return ORL_ERR_LAUNCH;
+  if (g_noalloc_dev[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ORL_ERR_LAUNCH;
+    g_noalloc_dev[dev] = static_cast<unsigned char*>(p);
+  }
+  unsigned char* scratch = g_noalloc_dev[dev];
+  int* err_dev = reinterpret_cast<int*>(scratch);
+  AttnWork* work_dev = reinterpret_cast<AttnWork*>(scratch + kNoAllocHeaderBytes);
+
+  // the same schedule as orl_attn_plan: segments by key count, descending (stable insertion sort into a static
+  // buffer), items of one (segment, head) adjacent
+  int n_order = 0;
+  for (int i = 0; i < n_seg; ++i) {
+    if (cu_q_host[i + 1] == cu_q_host[i]) continue;
+    const int lk = cu_k_host[i + 1] - cu_k_host[i];
+    int pos = n_order++;
+    while (pos > 0 && cu_k_host[g_noalloc_order[pos - 1] + 1] - cu_k_host[g_noalloc_order[pos - 1]] < lk) {
+      g_noalloc_order[pos] = g_noalloc_order[pos - 1];
+      --pos;
+    }
+    g_noalloc_order[pos] = i;
+  }
+  int n = 0;
+  for (int o = 0; o < n_order; ++o) {
+    const int i = g_noalloc_order[o];
+    const int lq = cu_q_host[i + 1] - cu_q_host[i], lk = cu_k_host[i + 1] - cu_k_host[i];
+    for (int h = 0; h < heads; ++h)
+      for (int p = 0; p < lq; p += 256) {
+        AttnWork& w = g_noalloc_items[n++];
+        w.q_row0 = cu_q_host[i] + p;
+        w.q_len = std::min(256, lq - p);
+        w.k_row0 = cu_k_host[i];
+        w.k_len = lk;
+        w.head = h;
+        w.seg = i;
+        w.pad0 = w.pad1 = 0;
+      }
+  }
+  if (cudaMemsetAsync(err_dev, 0, sizeof(int), stream) != cudaSuccess) return ORL_ERR_LAUNCH;
+  int rc = ORL_OK;
+  if (n > 0 && nq > 0) {
+    // pageable source: the call returns once the host buffer has been staged, so the next call may reuse it
+    if (cudaMemcpyAsync(work_dev, g_noalloc_items, static_cast<size_t>(n) * sizeof(AttnWork), cudaMemcpyHostToDevice,
+                        stream) != cudaSuccess)
+      return ORL_ERR_LAUNCH;
+    const void* kk = k;
+    const void* vv = v;
+    long long nkk = nk;
+    if (nk == 0) {   // every item has k_len 0 and loads nothing; the K/V maps only need a valid address
+      kk = vv = q;
+      nkk = nq;
+    }
+    rc = head_dim == 64 ? launch_attn<64>(q, kk, vv, out, lse, nq, nkk, heads, scale, work_dev, n, err_dev, stream)
+                        : launch_attn<128>(q, kk, vv, out, lse, nq, nkk, heads, scale, work_dev, n, err_dev, stream);
+    if (rc != ORL_OK) return rc;
+  }
+  if (status_host != nullptr) {
+    if (cudaMemcpyAsync(status_host, err_dev, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+      return ORL_ERR_LAUNCH;
+  }
+  return rc;
+}
