@@ -127,19 +127,21 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def make_inputs(lay, T, counts, H, Dh, dev, seed=0):
-    """Q/K RMS-normed over D from N(0, 1) (unit weight), V ~ N(0, 1), seeded on the CPU (BASELINE cfg2)"""
-    g = torch.Generator().manual_seed(seed)
+def make_inputs(lay, T, counts, H, Dh, dev, rows=None, seed=0):
+    """Q/K RMS-normed over D from N(0, 1) (unit weight), V ~ N(0, 1), seeded on the CPU (BASELINE cfg2); rows = the
+    rank's video token range (a, b), drawn from a generator seeded by (seed, a) so ranks draw only their own rows"""
+    g = torch.Generator().manual_seed(seed * 1000003 + (rows[0] if rows else 0))
     L, Nt = lay.n_frames * T, sum(counts)
+    a, b = rows or (0, L)
 
     def qk(n):
         x = torch.randn(n, H, Dh, generator=g)
         return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
-    q, k = qk(L), qk(L)
-    v = torch.randn(L, H, Dh, generator=g).to(torch.bfloat16)
+    q, k = qk(b - a), qk(b - a)
+    v = torch.randn(b - a, H, Dh, generator=g).to(torch.bfloat16)
     eq, ek = qk(Nt), qk(Nt)
     ev = torch.randn(Nt, H, Dh, generator=g).to(torch.bfloat16)
-    return [x.to(dev) for x in (q, k, v, eq, ek, ev)]
+    return [x.contiguous().to(dev) for x in (q, k, v, eq, ek, ev)]
 
 
 def main():
@@ -148,6 +150,8 @@ def main():
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--mode', default='auto', choices=['auto', 'scene', 'ulysses'],
+                    help='parallel path for N > 1 (auto = the Eq. 2 chooser)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small'],
                     help='small: the first two scenes of cfg2, for profiler captures (not a bench line)')
@@ -156,131 +160,136 @@ def main():
         return run_reference(args)
 
     from onereel_b200 import attention as A
+    from onereel_b200 import dist as D
+    from onereel_b200 import hunyuan15 as HY
     from onereel_b200 import scene as S
     from onereel_b200.csrc.build import build
+    from onereel_b200.pack import RunTable
     rank, world, local = dist_env()
-    build()
-    torch.cuda.set_device(local)
-    dev = torch.device('cuda', local)
+    if rank == 0:
+        build()
+    D.init('nccl')
     if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group('nccl', device_id=dev, timeout=timedelta(seconds=120))
+        D.barrier()
+        build()                      # other ranks load the library rank 0 built
+    dev = torch.device('cuda', local)
 
-    cfg = CFG2 if args.workload == 'cfg2' else SMALL
+    cfg = dict(CFG2 if args.workload == 'cfg2' else SMALL)
+    # weak scaling: N GPUs run cfg2's scene set repeated N times (per-GPU work fixed); every scene reads the frame
+    # memory of the first copy, so ranks exchange those rows (the path's real K/V gathering step)
+    cfg['lengths'] = cfg['lengths'] * world
     lay = cfg_layout(cfg)
     T, H, Dh = cfg['T'], cfg['heads'], cfg['dim']
     counts = [cfg['text']] * lay.n_scenes
-    L = lay.n_frames * T
-    q, k, v, eq, ek, ev = make_inputs(lay, T, counts, H, Dh, dev, seed=rank)
-    mine = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
-    segs = S.scene_segments(lay, T, counts, mine, set(range(lay.n_scenes)), (0, L))
-    plan = S.ScenePlan(segs, row_bytes=H * Dh * 2, heads=H, device=dev)
-    flops = sum(4.0 * a * b * H * Dh for a, b in zip(plan.lq, plan.lk))
-    ov, ot = torch.empty_like(q), torch.zeros_like(eq)
-    kp = q.new_empty(plan.n_keys, H, Dh)
-    vp = q.new_empty(plan.n_keys, H, Dh)
+    ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts}, fwd=1)
+    HY.plan_parallel(ctx, H)
+    own = ctx.own[rank]
+    q, k, v, eq, ek, ev = make_inputs(lay, T, counts, H, Dh, dev, own, seed=0)
+    proc = HY.Processor(ctx, 0)
     stream = torch.cuda.current_stream(dev)
-    ev_attn = []
 
-    def step(record=False):
-        plan.pack_kv(k, v, ek, ev, out=(kp, vp))
-        if record:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-        S.attend_segments(plan, q, eq, kp, vp, ov, ot)
-        if record:
-            b.record(stream)
-            ev_attn.append((a, b))
-
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
+    def step():
+        if ctx.run_mode == 'ulysses':
+            return proc.ulysses(q, k, v, eq, ek, ev)
+        return proc.scene(q, k, v, eq, ek, ev)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     A.check()
+    # useful FLOPs of this rank's segments (one timed pass of the instrumented launches)
+    S.TIMING = []
+    step()
+    torch.cuda.synchronize()
+    rank_flops = sum(f for _, _, f in S.TIMING)
+    S.TIMING = None
 
     with Clocks(local) as clk:
-        barrier()
+        D.barrier()
         torch.cuda.synchronize()
+        S.TIMING = []
+        packs0 = RunTable.launches
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(args.steps):
-            step(record=True)
+            step()
         t1.record(stream)
         torch.cuda.synchronize()
-        barrier()
+        D.barrier()
+    timing, S.TIMING = S.TIMING, None
+    n_launches = len(timing) + RunTable.launches - packs0
     A.check()
     ms = t0.elapsed_time(t1) / args.steps
-    attn_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_attn]))
+    attn_ms = sum(a.elapsed_time(b) for a, b, _ in timing) / args.steps
 
-    # end to end through the public API with host buffers: H2D of the layer's q/k/v/eq/ek/ev from pinned memory,
-    # the step, D2H of the outputs, every step inside the timed region
+    # end to end through the public API with host buffers: H2D of the layer's local q/k/v and the text q/k/v from
+    # pinned memory, the processor call, D2H of its outputs, every step inside the timed region
     host_in = [x.cpu().pin_memory() for x in (q, k, v, eq, ek, ev)]
-    host_out = [torch.empty(ov.shape, dtype=ov.dtype, pin_memory=True),
-                torch.empty(ot.shape, dtype=ot.dtype, pin_memory=True)]
     dev_in = [torch.empty_like(x) for x in (q, k, v, eq, ek, ev)]
+    host_out = [torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
+                torch.empty(eq.shape, dtype=eq.dtype, pin_memory=True)]
 
     def e2e_step():
-        for d, h in zip(dev_in, host_in):
-            d.copy_(h, non_blocking=True)
-        dq, dk, dv, deq, dek, dev_ = dev_in
-        kp2, vp2 = plan.pack_kv(dk, dv, dek, dev_, out=(kp, vp))
-        S.attend_segments(plan, dq, deq, kp2, vp2, ov, ot)
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        ov, ot = (proc.ulysses if ctx.run_mode == 'ulysses' else proc.scene)(*dev_in)
         host_out[0].copy_(ov, non_blocking=True)
         host_out[1].copy_(ot, non_blocking=True)
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
-    e_steps = max(3, args.steps // 2)
-    barrier()
+    e_steps = max(3, args.steps // 4)
+    D.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e_steps):
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    barrier()
+    D.barrier()
     A.check()
     e2e_ms = e0.elapsed_time(e1) / e_steps
 
+    total_flops = rank_flops
     if world > 1:
         import torch.distributed as dist
         t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, attn_ms, e2e_ms = t.tolist()
+        ms, attn_ms_max, e2e_ms = t.tolist()
+        f = torch.tensor([rank_flops], dtype=torch.float64, device=dev)
+        dist.all_reduce(f)
+        total_flops = f.item()
     if rank != 0:
-        if world > 1:
-            torch.distributed.destroy_process_group()
+        D.shutdown()
         return
     peak_burst, peak_sus, hbm, peak_kind = peaks()
-    achieved = flops / (attn_ms * 1e-3) / 1e12
+    achieved = rank_flops / (attn_ms * 1e-3) / 1e12
     cb = None
-    if not args.no_cpu_baseline and args.workload == 'cfg2':
+    if not args.no_cpu_baseline and args.workload == 'cfg2' and world == 1:
         cb, _ = cpu_baseline()
     h2d = sum(x.numel() * x.element_size() for x in host_in)
     d2h = sum(x.numel() * x.element_size() for x in host_out)
-    line = dict(metric=METRIC, value=world * flops / (ms * 1e-3) / 1e12, unit='TFLOP/s', n_gpus=world,
+    line = dict(metric=METRIC, value=total_flops / (ms * 1e-3) / 1e12, unit='TFLOP/s', n_gpus=world,
                 steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling='weak',
                 vs_baseline=None, dtype='bf16', data='synthetic (seeded; Q/K RMS-normed N(0,1), V N(0,1))',
-                config=dict(workload=f'{args.workload}: one HunyuanVideo-1.5-shaped scene-attention layer '
-                                     '(pack K/V + attention)',
-                            layout=cfg, segments=len(plan.segs), sum_q=sum(plan.lq), sum_k=sum(plan.lk),
-                            useful_tflop_per_step=flops / 1e12, parallelism=f'replicas x{world}' if world > 1 else 'single',
-                            l2='inputs larger than L2 (q/k/v 203 MB each, packed K/V 486 MB each)'),
-                e2e=dict(value=world * flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s', ms_per_step=e2e_ms,
+                config=dict(workload=(f'{args.workload}: one HunyuanVideo-1.5-shaped scene-attention layer through '
+                                      'hunyuan15.Processor.scene (pack K/V + attention' +
+                                      (', K/V exchange over NCCL' if world > 1 else '') + ')'),
+                            layout=dict(cfg, scenes=lay.n_scenes), run_mode=ctx.run_mode, path=ctx.path,
+                            own=ctx.own, useful_tflop_per_step=total_flops / 1e12,
+                            parallelism=(f'scene-parallel x{world} (weak: cfg2 scene set repeated per GPU)'
+                                         if world > 1 else 'single'),
+                            l2='inputs larger than L2 (q/k/v 203 MB each per GPU, packed K/V ~486 MB each)'),
+                e2e=dict(value=total_flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s', ms_per_step=e2e_ms,
                          h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
                 roofline=dict(bound='tensor', achieved=achieved, peak=peak_burst, unit='TFLOP/s',
                               frac=achieved / peak_burst, traffic=None,
-                              kernel='attn_fwd_kernel<128> (video + text launches per step)',
+                              frac_of_sustained=achieved / peak_sus if peak_sus else None,
+                              kernel='attn_fwd_kernel<128> (all attention launches of a step, rank 0)',
                               peak_source=f'{peak_kind} bf16 burst'),
-                gpu_launches=3 * args.steps, clocks=clk.summary(), cpu_baseline=cb)
+                gpu_launches=n_launches, clocks=clk.summary(), cpu_baseline=cb)
     print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    D.shutdown()
 
 
 if __name__ == '__main__':

@@ -122,6 +122,58 @@ ORL_API int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_v
 ORL_API int orl_lse_merge(void* o1, float* lse1, const void* o2, const float* lse2, long long n, long long ld_lse1,
                   long long ld_lse2, int heads, int head_dim, void* stream);
 
+/* ---------------------------------------------------------------- native planner (comm.py:18-112, layout.py:54-78) */
+
+/* A scene layout (layout.py:10-18 SceneLayout): lengths[n_scenes] latent frames per scene, halo frames of the
+ * neighbours on `sides` (0 'adj', 1 'prev', 2 'next'), extra frames per scene in CSR form
+ * (extra_frames[extra_offsets[j] .. extra_offsets[j + 1]]; both may be NULL for none). */
+typedef struct orl_layout {
+  const int32_t* lengths;
+  int32_t n_scenes;
+  int32_t halo;
+  int32_t sides;
+  const int32_t* extra_offsets;
+  const int32_t* extra_frames;
+} orl_layout;
+
+#define ORL_MODE_SCENE 0
+#define ORL_MODE_ULYSSES 1
+#define ORL_GRAN_BALANCED 0
+#define ORL_GRAN_TOKENS 1
+#define ORL_GRAN_SCENES 2
+
+/* Eq. 2 inputs and decision (comm.py:104-108). */
+typedef struct orl_path {
+  long long remote_rows; /* max over ranks of the K/V rows (per tensor) a rank gathers */
+  double V_G;            /* 2 * remote_rows */
+  double V_U;            /* 4 L (P - 1) / P^2 */
+  int32_t gather;        /* 1: 'scene' (K/V gathering), 0: 'ulysses' */
+} orl_path;
+
+/* Scene j's key frames: own frames, then halo and extra frames (layout.py:54-73). Returns the count, or
+ * -(count + 1000) when `frames` is NULL or too small. */
+ORL_API int orl_key_frames(const orl_layout* layout, int scene, int32_t* frames, int capacity);
+
+/* Per scene, the cost of one video query (comm.py:18-22): cost[n_scenes]; text may be NULL. */
+ORL_API int orl_query_cost(const orl_layout* layout, long long T, const int32_t* text, long long extra_keys,
+                           double* cost);
+
+/* Paper Algorithm 1 (comm.py:25-40): bounds[0..n] cuts of sum(sizes) queries into n work-balanced ranges. */
+ORL_API int orl_balanced(const int64_t* sizes, const double* cost, int n_scenes, int n, int64_t* bounds);
+
+/* Per-rank video token ranges (comm.py:43-66): bounds[0..n]; mode ORL_MODE_*, granularity ORL_GRAN_*. */
+ORL_API int orl_partition(const orl_layout* layout, long long T, int n, int mode, const int32_t* text,
+                          long long extra_keys, int granularity, int64_t* bounds);
+
+/* Token intervals outside [own_lo, own_hi) that the scenes intersecting it read (comm.py:88-96), plus the
+ * `extra` frames; intervals[2 * i], intervals[2 * i + 1]. Returns the count or -(count + 1000) if too small. */
+ORL_API int orl_needed(const orl_layout* layout, long long T, long long own_lo, long long own_hi, const int32_t* extra,
+                       int n_extra, int64_t* intervals, int capacity);
+
+/* Eq. 2 path choice for a partition (comm.py:99-112). */
+ORL_API int orl_choose_path(const orl_layout* layout, long long T, const int64_t* bounds, int n, double theta,
+                            const int32_t* extra, int n_extra, orl_path* path);
+
 #ifdef __cplusplus
 }
 #endif

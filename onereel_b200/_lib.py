@@ -6,11 +6,11 @@ CPU or library fallback.
 from __future__ import annotations
 
 import ctypes
-from pathlib import Path
+from pathlib import Path as _FsPath
 
 import numpy as np
 
-LIB_PATH = Path(__file__).resolve().parent / 'libonereel_b200.so'
+LIB_PATH = _FsPath(__file__).resolve().parent / 'libonereel_b200.so'
 
 c_int, c_ll, c_float, c_vp = ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_void_p
 P_I32 = ctypes.POINTER(ctypes.c_int32)
@@ -26,6 +26,18 @@ class CopyRun(ctypes.Structure):
     """orl_copy_run"""
     _fields_ = [('src_slot', ctypes.c_int32), ('dst_slot', ctypes.c_int32), ('src_off', ctypes.c_int64),
                 ('dst_off', ctypes.c_int64), ('vec0', ctypes.c_int64)]
+
+
+class Layout(ctypes.Structure):
+    """orl_layout"""
+    _fields_ = [('lengths', P_I32), ('n_scenes', ctypes.c_int32), ('halo', ctypes.c_int32), ('sides', ctypes.c_int32),
+                ('extra_offsets', P_I32), ('extra_frames', P_I32)]
+
+
+class Path(ctypes.Structure):
+    """orl_path"""
+    _fields_ = [('remote_rows', ctypes.c_longlong), ('V_G', ctypes.c_double), ('V_U', ctypes.c_double),
+                ('gather', ctypes.c_int32)]
 
 
 # numpy views of the same layouts (for building tables without Python loops over ctypes objects)
@@ -48,6 +60,12 @@ SIGNATURES = {
     'orl_pack_prepare': (c_ll, [c_vp, P_I64, c_int]),
     'orl_pack': (c_int, [c_vp, c_int, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
     'orl_lse_merge': (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_ll, c_int, c_int, c_vp]),
+    'orl_key_frames': (c_int, [c_vp, c_int, P_I32, c_int]),
+    'orl_query_cost': (c_int, [c_vp, c_ll, P_I32, c_ll, ctypes.POINTER(ctypes.c_double)]),
+    'orl_balanced': (c_int, [P_I64, ctypes.POINTER(ctypes.c_double), c_int, c_int, P_I64]),
+    'orl_partition': (c_int, [c_vp, c_ll, c_int, c_int, P_I32, c_ll, c_int, P_I64]),
+    'orl_needed': (c_int, [c_vp, c_ll, c_ll, c_ll, P_I32, c_int, P_I64, c_int]),
+    'orl_choose_path': (c_int, [c_vp, c_ll, P_I64, c_int, ctypes.c_double, P_I32, c_int, c_vp]),
 }
 
 _lib = None

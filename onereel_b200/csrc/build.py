@@ -1,7 +1,7 @@
 """Build libonereel_b200.so in-tree with nvcc for sm_100a (no torch extension machinery: a plain C-ABI library).
 
     python -m onereel_b200.csrc.build            # or build() from __graft_entry__.py
-Compiles every .cu of this directory with -gencode arch=compute_100a,code=sm_100a and links them into
+Compiles every .cu and .cpp of this directory with -gencode arch=compute_100a,code=sm_100a and links them into
 onereel_b200/libonereel_b200.so. Rebuilds only when a source or header is newer than the library.
 """
 from __future__ import annotations
@@ -14,7 +14,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 PKG = HERE.parent
 LIB = PKG / 'libonereel_b200.so'
-SOURCES = sorted(HERE.glob('*.cu'))
+SOURCES = sorted(HERE.glob('*.cu')) + sorted(HERE.glob('*.cpp'))
 HEADERS = sorted(HERE.glob('*.cuh')) + sorted(HERE.glob('*.h')) + sorted((PKG.parent / 'include').glob('*.h'))
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '-lineinfo', '-std=c++17', '--use_fast_math',

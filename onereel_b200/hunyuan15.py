@@ -1,0 +1,321 @@
+"""HunyuanVideo-1.5 scene attention on B200 — the reference's `onereel.models.hunyuan15` attention processor
+(src/onereel/models/hunyuan15.py:34-89 Context, 153-170 _segments, 173-303 Processor, 553-573 _plan_parallel).
+
+Same Context fields, same Processor(ctx, layer) with __call__ / scene / ulysses / _far_lse, same outputs. The device
+work per layer is: one gather/pack launch for the K/V of every local segment, one attention launch per query source
+(video rows of q, text rows of eq) writing straight into the output rows, and on several ranks the K/V exchange
+(grouped NCCL send/recv on the high-priority NCCL stream) overlapped with the attention of the scenes whose keys are
+all local. The segment list, run tables and work lists are compiled once per (layout, pass, partition) and cached.
+
+Variants the reference also carries but that are not on this path (bounded memory `memory`, `subject_links`, the Ring
+baseline `mode='ring'`, frame-memory selection) raise NotImplementedError here; `shared_pos='adjacent'` likewise.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from onereel_b200 import attention as A
+from onereel_b200 import comm, dist as D
+from onereel_b200 import scene as S
+from onereel_b200.layout import SceneLayout
+
+
+@dataclass
+class Context:
+    """hunyuan15.py:34-89 (same fields and defaults)"""
+    layout: SceneLayout
+    mode: str = 'scene'
+    partition: str = 'balanced'
+    theta: float = 1.0
+    cfg: bool = True
+    shared_pos: str = 'source'
+    shared_switch: int = 10
+    scene_rope: bool = False
+    rope_lengths: list = None
+    kv_chunks: int = 1
+    overlap: str = 'none'
+    text_sync: str = 'rows'
+    memory: int = 0
+    frame_memory: object = None
+    subject_links: int = 0
+    subject_step: int = 3
+    subject_layers: tuple = (18, 36)
+    subject_top: float = 0.2
+    T: int = 0
+    fwd: int = 0
+    counts: dict = field(default_factory=dict)
+    subj_tokens: list = field(default_factory=list)
+    subject: object = None
+    own: list = field(default_factory=list)
+    path: dict = field(default_factory=dict)
+    run_mode: str = 'scene'
+    ring: object = None
+    height: int = 480
+    width: int = 848
+    attn_override: object = None
+    forward_ms: list = field(default_factory=list)
+    vae_ms: list = field(default_factory=list)
+    _cache: dict = field(default_factory=dict)
+    _rot_full: tuple = None
+    _mem: object = None
+
+    def step(self) -> int:
+        return (self.fwd - 1) // 2 if self.cfg else self.fwd - 1
+
+    def cond(self) -> bool:
+        return (self.fwd - 1) % 2 == 0 if self.cfg else True
+
+    def text_ranges(self) -> list[tuple[int, int]]:
+        return S.text_ranges(self.counts[self.cond()])
+
+
+def _layout_key(lay: SceneLayout):
+    return (tuple(lay.lengths), lay.halo, lay.sides, tuple((j, tuple(sorted(v))) for j, v in sorted(lay.extra.items())))
+
+
+def _unsupported(ctx):
+    if ctx.memory or ctx.subject_links or ctx.run_mode == 'ring' or ctx.mode == 'ring':
+        raise NotImplementedError('bounded memory, subject links and the Ring baseline are not on the B200 path')
+    if ctx.shared_pos == 'adjacent' or (ctx.shared_pos == 'switch' and ctx.step() >= ctx.shared_switch):
+        raise NotImplementedError("shared_pos='adjacent' (shared-key RoPE re-rotation) is not on the B200 path")
+
+
+class _RankPlan:
+    """everything one rank needs for a scene-path layer: the pieces, the near / far segment plans (or the LSE
+    overlap's local / remote plans), the receive-buffer layout"""
+
+    def __init__(self, ctx, H, Dh, device, lse_overlap):
+        lay, T, counts = ctx.layout, ctx.T, ctx.counts[ctx.cond()]
+        r = D.rank()
+        own = ctx.own[r]
+        self.own = own
+        self.remote_index = (S.remote_index_of(lay, T, ctx.own, r, comm.needed) if D.world() > 1 else [])
+        mine, text_for = S.pieces(lay, T, own)
+        near = [p for p in mine if S.is_local(lay, T, own, p[0])]
+        far = [p for p in mine if not S.is_local(lay, T, own, p[0])]
+        rb = H * Dh * 2
+        mk = lambda g, side=None: (S.ScenePlan(S.scene_segments(lay, T, counts, g, text_for & {j for j, _ in g}, own,
+                                                                self.remote_index, side), rb, H, device) if g else None)
+        self.near = mk(near)
+        self.lse = lse_overlap and bool(far)
+        if self.lse:
+            self.far = None
+            self.far_local = mk(far, 'local')
+            self.far_remote = mk(far, 'remote')
+        else:
+            self.far = mk(far)
+            self.far_local = self.far_remote = None
+
+
+def _attend(plan, q, eq, k, v, ek, ev, ov, ot, rk=None, rv=None, lse_v=None, lse_t=None):
+    if plan is None or not plan.segs:
+        return
+    kp, vp = plan.pack_kv(k, v, ek, ev, rk, rv)
+    S.attend_segments(plan, q, eq, kp, vp, ov, ot, lse_v, lse_t)
+
+
+class Processor:
+    def __init__(self, ctx: Context, layer: int):
+        self.ctx, self.layer = ctx, layer
+
+    def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
+        """hunyuan15.py:177-210: projections, RMSNorm, RoPE on the local rows, bf16, scene / Ulysses attention,
+        output projections. `attn` is the diffusers Attention module (to_q/k/v, norm_q/k, add_*_proj, norm_added_*,
+        to_out, to_add_out)."""
+        ctx = self.ctx
+        _unsupported(ctx)
+        cos, sin = image_rotary_emb
+        ctx._rot_full = image_rotary_emb
+        a, b = ctx.own[D.rank()]
+        rot = (cos[a:b], sin[a:b])
+        q, k, v = (f(hidden_states).unflatten(2, (attn.heads, -1)) for f in (attn.to_q, attn.to_k, attn.to_v))
+        q, k = attn.norm_q(q), attn.norm_k(k)
+        q = apply_rotary_emb(q, rot)[0].to(torch.bfloat16).contiguous()
+        k = apply_rotary_emb(k, rot)[0].to(torch.bfloat16).contiguous()
+        v = v[0].to(torch.bfloat16).contiguous()
+        eq, ek, ev = (f(encoder_hidden_states).unflatten(2, (attn.heads, -1))
+                      for f in (attn.add_q_proj, attn.add_k_proj, attn.add_v_proj))
+        if getattr(attn, 'norm_added_q', None) is not None:
+            eq = attn.norm_added_q(eq)
+        if getattr(attn, 'norm_added_k', None) is not None:
+            ek = attn.norm_added_k(ek)
+        eq, ek, ev = (x[0].to(torch.bfloat16).contiguous() for x in (eq, ek, ev))
+        if ctx.run_mode == 'ulysses' or ctx.attn_override is not None:
+            hs, ehs = self.ulysses(q, k, v, eq, ek, ev)
+        else:
+            hs, ehs = self.scene(q, k, v, eq, ek, ev)
+        hs = attn.to_out[1](attn.to_out[0](hs.flatten(1, 2)[None].to(hidden_states.dtype)))
+        ehs = attn.to_add_out(ehs.flatten(1, 2)[None].to(hidden_states.dtype))
+        return hs, ehs
+
+    def _plan(self, H, Dh, device, lse_overlap):
+        ctx = self.ctx
+        key = ('scene', _layout_key(ctx.layout), ctx.T, tuple(ctx.counts[ctx.cond()]), tuple(map(tuple, ctx.own)),
+               D.rank(), H, Dh, str(device), lse_overlap)
+        plan = ctx._cache.get(key)
+        if plan is None:
+            plan = ctx._cache[key] = _RankPlan(ctx, H, Dh, device, lse_overlap)
+        return plan
+
+    def scene(self, q, k, v, eq, ek, ev):
+        """hunyuan15.py:212-251: the scenes of this rank's token range. The exchange is posted first; scenes whose keys
+        are all local attend while it is in flight; then the others (or, with overlap='lse', the others attend to
+        their local keys during the exchange and to the received keys after it, merged by log-sum-exp). kv_chunks
+        does not change the result (attention is per head) and a single exchange is posted on NVLink."""
+        ctx = self.ctx
+        _unsupported(ctx)
+        H, Dh = q.shape[1:]
+        lse_overlap = ctx.overlap == 'lse'
+        plan = self._plan(H, Dh, q.device, lse_overlap)
+        ex = comm.HaloExchange(ctx.layout, ctx.own, ctx.T, k, v) if D.world() > 1 else None
+        if ex is not None and ex.remote_index != plan.remote_index:
+            raise RuntimeError('exchange layout differs from the compiled plan')
+        ov, ot = torch.empty_like(q), torch.zeros_like(eq)
+        _attend(plan.near, q, eq, k, v, ek, ev, ov, ot)
+        if plan.lse:
+            self._far_lse(plan, ex, q, eq, k, v, ek, ev, ov, ot)
+        else:
+            if ex is not None:
+                ex.wait()
+            _attend(plan.far, q, eq, k, v, ek, ev, ov, ot, ex.remote_k if ex else None, ex.remote_v if ex else None)
+        if ctx.text_sync == 'all_reduce' or D.world() == 1:
+            D.all_reduce(ot)
+        else:
+            comm.send_text_rows(ot, ctx.layout, ctx.own, ctx.T, ctx.text_ranges())
+        return ov, ot
+
+    def _far_lse(self, plan, ex, q, eq, k, v, ek, ev, ov, ot):
+        """hunyuan15.py:253-277: far pieces attend to their local keys (and text) while the exchange is in flight, then
+        to the received keys; the two partial results are merged by log-sum-exp (orl_lse_merge)"""
+        H = q.shape[1]
+        lse_v = torch.empty(H, q.shape[0], dtype=torch.float32, device=q.device)
+        lse_t = torch.empty(H, eq.shape[0], dtype=torch.float32, device=q.device)
+        _attend(plan.far_local, q, eq, k, v, ek, ev, ov, ot, lse_v=lse_v, lse_t=lse_t)
+        if ex is not None:
+            ex.wait()
+        fr = plan.far_remote
+        if fr is None or not fr.segs:
+            return
+        o2v, o2t = torch.empty_like(q), torch.empty_like(eq)
+        l2v = torch.empty_like(lse_v)
+        l2t = torch.empty_like(lse_t)
+        _attend(fr, q, eq, k, v, ek, ev, o2v, o2t, ex.remote_k, ex.remote_v, l2v, l2t)
+        for s in fr.segs:
+            lo, hi = s.q[1], s.q[2]
+            if s.kind == 'v':
+                A.lse_merge(ov[lo:hi], lse_v[:, lo:hi], o2v[lo:hi], l2v[:, lo:hi])
+            else:
+                A.lse_merge(ot[lo:hi], lse_t[:, lo:hi], o2t[lo:hi], l2t[:, lo:hi])
+
+    def ulysses(self, q, k, v, eq, ek, ev):
+        """hunyuan15.py:279-303: heads redistributed by all-to-all; every scene on the local heads; text outputs of the
+        local heads all-reduced"""
+        ctx = self.ctx
+        n, r, H = D.world(), D.rank(), q.shape[1]
+        sl = slice(r * H // n, (r + 1) * H // n)
+        qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
+        eqs, eks, evs = (x[:, sl].contiguous() for x in (eq, ek, ev))
+        if ctx.attn_override is not None:
+            res = ctx.attn_override(self.layer, qa, ka, va, eqs, eks, evs)
+            if res is not None:
+                ot = eq.new_zeros(eq.shape)
+                ot[:, sl] = res[1]
+                D.all_reduce(ot)
+                return comm.a2a_tokens(res[0]), ot
+        Hl, Dh = qa.shape[1:]
+        lay, T = ctx.layout, ctx.T
+        L = lay.n_frames * T
+        key = ('ulysses', _layout_key(lay), T, tuple(ctx.counts[ctx.cond()]), Hl, Dh, str(q.device))
+        plan = ctx._cache.get(key)
+        if plan is None:
+            scenes = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
+            plan = ctx._cache[key] = S.ScenePlan(
+                S.scene_segments(lay, T, ctx.counts[ctx.cond()], scenes, set(range(lay.n_scenes)), (0, L)),
+                Hl * Dh * 2, Hl, q.device)
+        ov = torch.empty_like(qa)
+        otl = torch.zeros_like(eqs)
+        _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl)
+        ot = eq.new_zeros(eq.shape)
+        ot[:, sl] = otl
+        D.all_reduce(ot)
+        return comm.a2a_tokens(ov), ot
+
+
+def apply_rotary_emb(x, freqs):
+    """real-valued rotary embedding over interleaved pairs (diffusers' apply_rotary_emb with use_real=True,
+    use_real_unbind_dim=-1, sequence_dim=1): x [B, S, H, D], cos / sin [S, D]"""
+    cos, sin = (f[None, :, None, :].to(x.device) for f in freqs)
+    xr, xi = x.float().unflatten(-1, (-1, 2)).unbind(-1)
+    rot = torch.stack([-xi, xr], -1).flatten(-2)
+    return (x.float() * cos + rot * sin).to(x.dtype)
+
+
+def plan_parallel(ctx: Context, heads: int):
+    """hunyuan15.py:553-573: the work-balanced partition (Algorithm 1) for K/V gathering, equal ranges for Ulysses;
+    'auto' takes the gathering path when Eq. 2 says it moves less (and when Ulysses cannot split frames or heads)"""
+    n, lay = D.world(), ctx.layout
+    ctx.ring = None
+    if n == 1:
+        ctx.run_mode, ctx.own, ctx.path = 'scene', [(0, lay.n_frames * ctx.T)], {}
+        return
+    _unsupported(ctx)
+    gather = comm.partition(lay, n, ctx.T, 'scene', ctx.counts[True], ctx.memory, ctx.partition)
+    ctx.path = comm.choose_path(lay, gather, ctx.T, ctx.theta)
+    ctx.path['ulysses_ok'] = lay.n_frames * ctx.T % n == 0 and heads % n == 0
+    ctx.run_mode = ctx.mode if ctx.mode != 'auto' else ctx.path['path'] if ctx.path['ulysses_ok'] else 'scene'
+    assert ctx.run_mode != 'ulysses' or ctx.path['ulysses_ok'], f'Ulysses needs video tokens and heads divisible by {n}'
+    ctx.own = gather if ctx.run_mode == 'scene' else comm.partition(lay, n, ctx.T, 'ulysses')
+
+
+_plan_parallel = plan_parallel      # the reference's private name (hunyuan15.py:553)
+
+
+def _segments(ctx, scenes, qf, kf, vf, eq, ek, ev, text_for):
+    """hunyuan15.py:153-170 on tensors (API compatibility; the processors use the compiled plans instead): packed
+    (q, k, v) per scene piece and its meta"""
+    lay, tr = ctx.layout, ctx.text_ranges()
+    segs, meta = [], []
+    for j, (qlo, qhi) in scenes:
+        t0, t1 = tr[j]
+        keys = lay.key_frames(j)
+        segs.append((qf(qlo, qhi), torch.cat([kf(keys), ek[t0:t1]]), torch.cat([vf(keys), ev[t0:t1]])))
+        meta.append(('v', j, qlo, qhi))
+        if j in text_for:
+            fr = lay.frames[j]
+            segs.append((eq[t0:t1], torch.cat([kf(fr), ek[t0:t1]]), torch.cat([vf(fr), ev[t0:t1]])))
+            meta.append(('t', j, t0, t1))
+    return segs, meta
+
+
+def local_rows(ctx):
+    """hunyuan15.py:457-460: this rank's video rows"""
+    a, b = ctx.own[D.rank()]
+    return slice(a, b)
+
+
+def gather_rows(ctx, x):
+    """hunyuan15.py:463-466: [B, local rows, C] -> [B, all tokens, C]"""
+    return comm.gather_tokens(x, ctx.own)
+
+
+def install_attention(transformer, ctx: Context):
+    """the attention part of hunyuan15.install (407-440): a Processor on every block, the forward counter, and the
+    token shard / gather hooks of the first / last block when parallel. `transformer` is the diffusers
+    HunyuanVideo15Transformer3DModel (or any module with .transformer_blocks[i].attn.set_processor)."""
+    for i, blk in enumerate(transformer.transformer_blocks):
+        blk.attn.set_processor(Processor(ctx, i))
+
+    def pre(m, args, kw):
+        ctx.fwd += 1
+    transformer.register_forward_pre_hook(pre, with_kwargs=True)
+    if D.world() > 1:
+        def shard(m, args):
+            return (args[0][:, local_rows(ctx)],) + tuple(args[1:])
+
+        def gather(m, args, out):
+            return gather_rows(ctx, out[0]), out[1]
+        transformer.transformer_blocks[0].register_forward_pre_hook(shard)
+        transformer.transformer_blocks[-1].register_forward_hook(gather)

@@ -16,6 +16,7 @@ from onereel_b200 import _lib as L
 
 class RunTable:
     """a prepared run table on one device: runs_dev (uint8 view of orl_copy_run [n]), total 16-byte vectors"""
+    launches = 0          # pack launches issued by this process (benchmark launch accounting)
 
     def __init__(self, src_slot, dst_slot, src_off, dst_off, nbytes, device):
         n = len(nbytes)
@@ -37,6 +38,7 @@ class RunTable:
         SrcArr = L.c_vp * len(src_bases)
         s = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
         n_seg = 0 if seg_len_dev is None else seg_len_dev.numel()
+        RunTable.launches += 1
         L.check(L.lib().orl_pack(self.dev.data_ptr() if self.dev is not None else None, self.n_runs, self.total_vecs,
                                  n_planes, n_slots, SrcArr(*src_bases), SrcArr(*dst_bases),
                                  None if seg_len_dev is None else seg_len_dev.data_ptr(), n_seg,

@@ -8,8 +8,8 @@ the segment list with Python loops and torch.cat copies in every layer; here the
 
   - a K/V run table: per segment, its key rows as row runs from the sources (this rank's video rows, the received
     exchange buffers, the text rows), executed by the pack kernel for K and V in one launch (two planes);
-  - the query rows read in place: video queries straight from the rank's q, text queries from eq — no q pack;
-  - an output scatter run table (packed text outputs -> their rows of ot; video outputs are written in place);
+  - the query rows read in place (video queries straight from the rank's q, text queries from eq) and the outputs
+    written in place (video rows of ov, text rows of ot): no q pack and no output scatter;
   - the attention work list and cu_seqlens (bit-exact with attention.cu_seqlens of the reference's call).
 
 Packed segment order (must match the reference, pinned by tests/golden/segments.json): per scene piece j ascending,
@@ -69,23 +69,26 @@ def text_ranges(counts) -> list[tuple[int, int]]:
     return [(int(c[j]), int(c[j + 1])) for j in range(len(counts))]
 
 
-def video_key_runs(frames, T, own, remote_index):
+def video_key_runs(frames, T, own, remote_index, side=None):
     """token intervals of a frame list -> source runs: rows inside own = (a, b) come from the local rows, the others
-    from the received buffer intervals (remote_index: sorted [(token lo, token hi, buffer row of lo)])"""
+    from the received buffer intervals (remote_index: sorted [(token lo, token hi, buffer row of lo)]).
+    side 'local' / 'remote' keeps only the local / received runs (comm.py:180-201 `rows(i, side)`)."""
     a, b = own
     runs = []
     for lo, hi in frame_tokens(frames, T):
         while lo < hi:
             if a <= lo < b:
                 e = min(hi, b)
-                runs.append((VIDEO, lo - a, e - a))
+                if side != 'remote':
+                    runs.append((VIDEO, lo - a, e - a))
             else:
                 hit = next(((x, y, r) for x, y, r in remote_index if x <= lo < y), None)
                 if hit is None:
                     raise ValueError(f'token {lo} is neither local ({a}, {b}) nor received')
                 x, y, r = hit
                 e = min(hi, y)
-                runs.append((REMOTE, r + lo - x, r + e - x))
+                if side != 'local':
+                    runs.append((REMOTE, r + lo - x, r + e - x))
             lo = e
     return _merge_runs(runs)
 
@@ -102,22 +105,59 @@ def _merge_runs(runs):
     return out
 
 
-def scene_segments(layout, T, counts, scenes, text_for, own, remote_index=()):
+def scene_segments(layout, T, counts, scenes, text_for, own, remote_index=(), side=None):
     """the packed segments of `scenes` [(j, (token lo, token hi))] on a rank owning video tokens own = (a, b);
-    text_for: scenes whose text queries this call runs (hunyuan15.py:153-170)"""
+    text_for: scenes whose text queries this call runs (hunyuan15.py:153-170). counts None: no joint text (Wan).
+    side None: every key; 'local': local video keys and the text (the first pass of the LSE overlap,
+    hunyuan15.py:258-260); 'remote': received video keys only (its second pass, 262-268; segments without any are
+    dropped)."""
     tr = text_ranges(counts) if counts is not None else None
     a = own[0]
     segs = []
     for j, (qlo, qhi) in scenes:
-        kv = video_key_runs(layout.key_frames(j), T, own, remote_index)
-        if tr is not None and tr[j][1] > tr[j][0]:
+        kv = video_key_runs(layout.key_frames(j), T, own, remote_index, side)
+        if tr is not None and tr[j][1] > tr[j][0] and side != 'remote':
             kv = kv + [(TEXT, tr[j][0], tr[j][1])]
-        segs.append(Segment('v', j, (VIDEO, qlo - a, qhi - a), kv, ('v', qlo - a, qhi - a)))
+        if kv or side is None:
+            segs.append(Segment('v', j, (VIDEO, qlo - a, qhi - a), kv, ('v', qlo - a, qhi - a)))
         if tr is not None and j in text_for:
             t0, t1 = tr[j]
-            kv_t = video_key_runs(layout.frames[j], T, own, remote_index) + [(TEXT, t0, t1)]
-            segs.append(Segment('t', j, (TEXT, t0, t1), kv_t, ('t', t0, t1)))
+            kv_t = video_key_runs(layout.frames[j], T, own, remote_index, side)
+            if side != 'remote':
+                kv_t = kv_t + [(TEXT, t0, t1)]
+            if kv_t or side is None:
+                segs.append(Segment('t', j, (TEXT, t0, t1), kv_t, ('t', t0, t1)))
     return segs
+
+
+def is_local(layout, T, own, j) -> bool:
+    """hunyuan15.py:224: every key frame of scene j lies in the rank's own token range"""
+    a, b = own
+    return all(a <= lo and hi <= b for lo, hi in frame_tokens(layout.key_frames(j), T))
+
+
+def pieces(layout, T, own):
+    """hunyuan15.py:222-223: scene pieces of a rank's token range and the scenes whose text queries it runs"""
+    a, b = own
+    mine = [(j, (max(lo * T, a), min(hi * T, b))) for j, (lo, hi) in enumerate(layout.ranges)
+            if lo * T < b and hi * T > a]
+    text_for = {j for j, (lo, _) in enumerate(layout.ranges) if a <= lo * T < b}
+    return mine, text_for
+
+
+def remote_index_of(layout, T, own_all, r, needed_fn):
+    """the receive-buffer layout of comm.HaloExchange for rank r: [(token lo, token hi, buffer row)] sorted by lo"""
+    need = needed_fn(layout, T, own_all[r])
+    recv = []
+    for p, (a, b) in enumerate(own_all):
+        if p == r:
+            continue
+        recv += [(max(lo, a), min(hi, b)) for lo, hi in need if lo < b and hi > a]
+    out, off = [], 0
+    for lo, hi in sorted(recv):
+        out.append((lo, hi, off))
+        off += hi - lo
+    return out
 
 
 @dataclass
@@ -169,10 +209,14 @@ class ScenePlan:
         return kp, vp
 
 
+# Optional launch timing for benchmarks: when TIMING is a list, every attention launch appends (start, end) CUDA
+# events recorded on its stream, with the useful FLOPs it computes.
+TIMING = None
+
+
 def attend_segments(plan: ScenePlan, q, eq, kp, vp, ov, ot, lse_v=None, lse_t=None):
     """attention of every segment of the plan: queries read in place from q (video) and eq (text). Video outputs go
-    straight to their rows of ov; text outputs are computed into their rows of ot. One kernel launch per query
-    source (video, text)."""
+    straight to their rows of ov; text outputs straight to their rows of ot. One kernel launch per query source."""
     for kind, qsrc, dst, lse in (('v', q, ov, lse_v), ('t', eq, ot, lse_t)):
         idx = [i for i, s in enumerate(plan.segs) if s.kind == kind]
         if not idx:
@@ -181,4 +225,12 @@ def attend_segments(plan: ScenePlan, q, eq, kp, vp, ov, ot, lse_v=None, lse_t=No
         ql = [plan.segs[i].lq for i in idx]
         ks = [plan.cu_k[i] for i in idx]
         kl = [plan.lk[i] for i in idx]
+        if TIMING is not None:
+            stream = torch.cuda.current_stream(qsrc.device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
         A.attend(qsrc, kp, vp, qs, ql, ks, kl, out=dst, lse=lse)
+        if TIMING is not None:
+            e1.record(stream)
+            H, Dh = qsrc.shape[1:]
+            TIMING.append((e0, e1, sum(4.0 * a * b * H * Dh for a, b in zip(ql, kl))))

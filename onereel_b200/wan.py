@@ -1,0 +1,165 @@
+"""Wan2.2 self-attention on B200 — the reference's `onereel.models.wan` processor (src/onereel/models/wan.py:33-58
+Context, 64-74 _qk, 77-173 Processor, 248-271 _plan_parallel).
+
+Self-attention has no joint text. One GPU / Ulysses: `ranges` — every scene's keys are one contiguous token range
+(scene plus adjacent halo), read in place by the attention kernel (orl_attn_plan_ranges: no copy), or packed per
+scene by the gather/pack kernel when the scene also reads frame-memory frames. K/V gathering: `scene`, as Hunyuan's
+without text. Cross-attention (per scene on its sentence) stays the model's own processor, as in the reference.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from onereel_b200 import attention as A
+from onereel_b200 import comm, dist as D
+from onereel_b200 import scene as S
+from onereel_b200.hunyuan15 import _attend, _layout_key
+from onereel_b200.layout import SceneLayout
+
+TEXT_LEN = 512
+
+
+@dataclass
+class Context:
+    """wan.py:33-58 (same fields and defaults)"""
+    layout: SceneLayout
+    mode: str = 'scene'
+    theta: float = 1.0
+    kv_chunks: int = 1
+    memory: int = 0
+    frame_memory: object = None
+    T: int = 0
+    fwd: int = 0
+    own: list = field(default_factory=list)
+    path: dict = field(default_factory=dict)
+    run_mode: str = 'scene'
+    ring: object = None
+    height: int = 704
+    width: int = 1280
+    cfg: bool = False
+    attn_override: object = None
+    _mem: object = None
+    _cache: dict = field(default_factory=dict)
+
+    def cond(self) -> bool:
+        return (self.fwd - 1) % 2 == 0 if self.cfg else True
+
+    def step(self) -> int:
+        return (self.fwd - 1) // 2 if self.cfg else self.fwd - 1
+
+
+def qk_norm_rope(q, k, wq, wk, eps: float, cos, sin, heads: int):
+    """wan.py:64-74: RMSNorm over the hidden dimension, then the interleaved RoPE of diffusers' Wan attention"""
+    def norm(x, w):
+        return F.rms_norm(x, (x.shape[-1],), w, eps)
+
+    def rope(x):
+        x1, x2 = x.unflatten(-1, (-1, 2)).unbind(-1)
+        c, s_ = cos[..., 0::2], sin[..., 1::2]
+        return torch.stack([x1 * c - x2 * s_, x1 * s_ + x2 * c], -1).flatten(-2).type_as(x)
+    return rope(norm(q, wq).unflatten(2, (heads, -1))), rope(norm(k, wk).unflatten(2, (heads, -1)))
+
+
+class Processor:
+    def __init__(self, ctx: Context, kind: str, orig, layer: int):
+        self.ctx, self.kind, self.orig, self.layer = ctx, kind, orig, layer
+
+    def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, rotary_emb=None):
+        """wan.py:81-108"""
+        ctx, T, lay = self.ctx, self.ctx.T, self.ctx.layout
+        if ctx.memory or ctx.run_mode == 'ring':
+            raise NotImplementedError('bounded memory and the Ring baseline are not on the B200 path')
+        a, b = ctx.own[D.rank()]
+        if self.kind == 'cross':
+            pieces = [(j, lo - a, hi - a) for j, (lo, hi) in [(j, (max(lo * T, a), min(hi * T, b)))
+                                                              for j, (lo, hi) in enumerate(lay.ranges)
+                                                              if lo * T < b and hi * T > a]]
+            return torch.cat([self.orig(attn, hidden_states[:, lo:hi],
+                                        encoder_hidden_states[:, j * TEXT_LEN:(j + 1) * TEXT_LEN], None, rotary_emb)
+                              for j, lo, hi in pieces], 1)
+        cos, sin = (x[:, a:b] for x in rotary_emb)
+        q, k, v = attn.to_q(hidden_states), attn.to_k(hidden_states), attn.to_v(hidden_states)
+        q, k = qk_norm_rope(q, k, attn.norm_q.weight, attn.norm_k.weight, attn.norm_q.eps, cos, sin, attn.heads)
+        v = v.unflatten(2, (attn.heads, -1))
+        q, k, v = (x[0].to(torch.bfloat16).contiguous() for x in (q, k, v))
+        if ctx.attn_override is not None:
+            qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
+            r = ctx.attn_override(self.layer, qa, ka, va)
+            o = comm.a2a_tokens(self.ranges(qa, ka, va) if r is None else r)
+        elif ctx.run_mode == 'ulysses' or D.world() == 1:
+            o = comm.a2a_tokens(self.ranges(comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)))
+        else:
+            o = self.scene(q, k, v)
+        return attn.to_out[1](attn.to_out[0](o.flatten(1, 2)[None].type_as(hidden_states)))
+
+    def ranges(self, q, k, v):
+        """wan.py:110-124: all tokens; every scene's keys one contiguous range read in place, or packed per scene when
+        it reads extra frames"""
+        T, lay = self.ctx.T, self.ctx.layout
+        if any(lay.extra.get(j) for j in range(lay.n_scenes)):
+            H, Dh = q.shape[1:]
+            L = lay.n_frames * T
+            key = ('wan_ranges', _layout_key(lay), T, H, Dh, str(q.device))
+            plan = self.ctx._cache.get(key)
+            if plan is None:
+                scenes = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
+                plan = self.ctx._cache[key] = S.ScenePlan(S.scene_segments(lay, T, None, scenes, set(), (0, L)),
+                                                          H * Dh * 2, H, q.device)
+            o = torch.empty_like(q)
+            _attend(plan, q, None, k, v, None, None, o, None)
+            return o
+        q_ranges = [(lo * T, hi * T) for lo, hi in lay.ranges]
+        k_ranges = [(a * T, b * T) for a, b in (lay.key_range(j) for j in range(lay.n_scenes))]
+        for j, (a, b) in enumerate(lay.key_range(j) for j in range(lay.n_scenes)):
+            assert b - a == len(lay.key_frames(j)), 'halo must be contiguous with its scene'
+        return A.overlapping_ranges(q, k, v, q_ranges, k_ranges)
+
+    def scene(self, q, k, v):
+        """wan.py:126-152: K/V gathering; scenes whose keys are all local attend while the exchange is in flight"""
+        ctx, T, lay = self.ctx, self.ctx.T, self.ctx.layout
+        H, Dh = q.shape[1:]
+        r = D.rank()
+        own = ctx.own[r]
+        key = ('wan_scene', _layout_key(lay), T, tuple(map(tuple, ctx.own)), r, H, Dh, str(q.device))
+        plans = ctx._cache.get(key)
+        if plans is None:
+            rindex = S.remote_index_of(lay, T, ctx.own, r, comm.needed) if D.world() > 1 else []
+            mine, _ = S.pieces(lay, T, own)
+            near = [p for p in mine if S.is_local(lay, T, own, p[0])]
+            far = [p for p in mine if not S.is_local(lay, T, own, p[0])]
+            mk = lambda g: S.ScenePlan(S.scene_segments(lay, T, None, g, set(), own, rindex), H * Dh * 2, H,
+                                       q.device) if g else None
+            plans = ctx._cache[key] = (rindex, mk(near), mk(far))
+        rindex, near, far = plans
+        ex = comm.HaloExchange(lay, ctx.own, T, k, v) if D.world() > 1 else None
+        if ex is not None and ex.remote_index != rindex:
+            raise RuntimeError('exchange layout differs from the compiled plan')
+        ov = torch.empty_like(q)
+        _attend(near, q, None, k, v, None, None, ov, None)
+        if ex is not None:
+            ex.wait()
+        _attend(far, q, None, k, v, None, None, ov, None, ex.remote_k if ex else None, ex.remote_v if ex else None)
+        return ov
+
+
+def plan_parallel(ctx: Context, heads: int):
+    """wan.py:248-271"""
+    n, lay = D.world(), ctx.layout
+    ctx.ring = None
+    if n == 1:
+        ctx.run_mode, ctx.own, ctx.path = 'scene', [(0, lay.n_frames * ctx.T)], {}
+        return
+    if ctx.memory or ctx.mode == 'ring':
+        raise NotImplementedError('bounded memory and the Ring baseline are not on the B200 path')
+    gather = comm.partition(lay, n, ctx.T, 'scene', None, ctx.memory)
+    ctx.path = comm.choose_path(lay, gather, ctx.T, ctx.theta)
+    ctx.path['ulysses_ok'] = lay.n_frames * ctx.T % n == 0 and heads % n == 0
+    ctx.run_mode = ctx.mode if ctx.mode != 'auto' else ctx.path['path'] if ctx.path['ulysses_ok'] else 'scene'
+    assert ctx.run_mode != 'ulysses' or ctx.path['ulysses_ok'], f'Ulysses needs video tokens and heads divisible by {n}'
+    ctx.own = gather if ctx.run_mode == 'scene' else comm.partition(lay, n, ctx.T, 'ulysses')
+
+
+_plan_parallel = plan_parallel

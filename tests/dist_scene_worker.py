@@ -1,0 +1,102 @@
+"""Multi-GPU parity worker (run by tests/test_gpu_dist.py under torchrun, one process per GPU, NCCL):
+  python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P tests/dist_scene_worker.py
+
+Every rank builds the same full tensors from a seeded CPU generator, keeps its partition's rows and runs the parallel
+path; the single-GPU result of the same layer is computed on every rank from the full tensors. Checks (the reference's
+tests/dist_onereel_kv_chunks.py, dist_onereel_overlap.py, dist_onereel_gather.py):
+  - K/V gathering (Hunyuan and Wan) equals the single-GPU result bit for bit (video rows and the text rows of the
+    scenes the rank touches), with halo and frame-memory frames, boundaries inside frames;
+  - overlap='lse' (local keys during the exchange, LSE merge) within rel 1e-2 of waiting;
+  - Ulysses equals the single-GPU result bit for bit; text_sync='all_reduce' equals 'rows' on touched scenes;
+  - the Eq. 2 chooser ('auto') picks a path and reproduces the single-GPU result.
+Prints PASS lines on rank 0; any failure raises (non-zero exit)."""
+import os
+import sys
+from pathlib import Path
+
+import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+from onereel_b200 import attention as A, comm, dist as D, hunyuan15 as HY, wan as WN   # noqa: E402
+from onereel_b200.layout import SceneLayout                                            # noqa: E402
+
+
+def main():
+    D.init('nccl', timeout_s=60)
+    r, n = D.rank(), D.world()
+    T, H, Dh = 64, 16, 128
+    rel = lambda x, y: ((x.float() - y.float()).norm() / y.float().norm()).item()
+    cases = (([3, 5, 2, 4, 6], 0, True), ([10, 1, 1, 2], 2, False), ([2, 2, 2, 2, 2, 2], 1, False),
+             ([5, 2, 7], 0, True), ([4, 4, 4, 4, 4, 4, 4, 4], 2, True))
+    mid = 0
+    for lengths, halo, extra in cases:
+        g = torch.Generator().manual_seed(len(lengths))
+        rnd = lambda *s: torch.randn(*s, generator=g).to('cuda', torch.bfloat16)
+        lay = SceneLayout(lengths, halo=halo)
+        if extra:
+            lay.extra = {j: [(7 * j + 3) % lay.n_frames, lay.n_frames - 1] for j in range(lay.n_scenes)}
+        L = lay.n_frames * T
+        counts = [3 + j for j in range(lay.n_scenes)]
+        q, k, v = rnd(L, H, Dh), rnd(L, H, Dh), rnd(L, H, Dh)
+        eq, ek, ev = (rnd(sum(counts), H, Dh) for _ in range(3))
+        # single-GPU reference on every rank (own = everything, world treated as 1)
+        saved = D.world, D.rank
+        D.world, D.rank = (lambda: 1), (lambda: 0)
+        c1 = HY.Context(lay, T=T, own=[(0, L)], counts={True: counts}, fwd=1)
+        ref_v, ref_t = HY.Processor(c1, 0).scene(q, k, v, eq, ek, ev)
+        wref = WN.Processor(WN.Context(lay, T=T, own=[(0, L)]), 'self', None, 0).ranges(q, k, v)
+        D.world, D.rank = saved
+        own = comm.partition(lay, n, T, 'scene', counts)
+        a, b = own[r]
+        mid += any(x % T for x, _ in own[1:])
+        ql, kl, vl = (x[a:b].contiguous() for x in (q, k, v))
+        touched = [j for j, (lo, hi) in enumerate(lay.ranges) if lo * T < b and hi * T > a]
+        tr = HY.S.text_ranges(counts)
+        trows = torch.cat([torch.arange(*tr[j]) for j in touched]) if touched else torch.arange(0)
+        res = {}
+        for overlap in ('none', 'lse'):
+            for sync in ('rows', 'all_reduce'):
+                ctx = HY.Context(lay, T=T, own=own, counts={True: counts}, fwd=1, overlap=overlap, text_sync=sync)
+                res[overlap, sync] = HY.Processor(ctx, 0).scene(ql, kl, vl, eq, ek, ev)
+        hv, ht = res['none', 'rows']
+        assert torch.equal(hv, ref_v[a:b]), (lengths, r, 'hunyuan video')
+        assert torch.equal(ht[trows], ref_t[trows]), (lengths, r, 'hunyuan text')
+        assert torch.equal(res['none', 'all_reduce'][1], ref_t), (lengths, r, 'all_reduce text')
+        lv, lt = res['lse', 'rows']
+        assert rel(lv, ref_v[a:b]) < 1e-2 and rel(lt[trows], ref_t[trows]) < 1e-2, (lengths, r, 'lse')
+        wc = WN.Context(lay, T=T, own=own)
+        wv = WN.Processor(wc, 'self', None, 0).scene(ql, kl, vl)
+        assert torch.equal(wv, wref[a:b]), (lengths, r, 'wan video')
+        # Ulysses: equal split, heads redistributed
+        if L % n == 0 and H % n == 0:
+            uown = comm.partition(lay, n, T, 'ulysses')
+            ua, ub = uown[r]
+            uc = HY.Context(lay, T=T, own=uown, counts={True: counts}, fwd=1, run_mode='ulysses')
+            uv, ut = HY.Processor(uc, 0).ulysses(*(x[ua:ub].contiguous() for x in (q, k, v)), eq, ek, ev)
+            assert torch.equal(uv.contiguous(), ref_v[ua:ub]), (lengths, r, 'ulysses video')
+            assert torch.equal(ut, ref_t), (lengths, r, 'ulysses text')
+            wu = WN.Processor(WN.Context(lay, T=T, own=uown), 'self', None, 0)
+            wo = comm.a2a_tokens(wu.ranges(*(comm.a2a_heads(x[ua:ub].contiguous()) for x in (q, k, v))))
+            assert torch.equal(wo.contiguous(), wref[ua:ub]), (lengths, r, 'wan ulysses')
+        # the Eq. 2 chooser
+        actx = HY.Context(lay, mode='auto', T=T, counts={True: counts}, fwd=1)
+        HY.plan_parallel(actx, H)
+        aa, ab = actx.own[r]
+        args = [x[aa:ab].contiguous() for x in (q, k, v)] + [eq, ek, ev]
+        av, at = (HY.Processor(actx, 0).ulysses(*args) if actx.run_mode == 'ulysses'
+                  else HY.Processor(actx, 0).scene(*args))
+        assert torch.equal(av.contiguous(), ref_v[aa:ab]), (lengths, r, 'auto', actx.run_mode)
+        torch.cuda.synchronize()
+        A.check()
+        if r == 0:
+            print(f'PASS n={n} {lengths} halo={halo} extra={extra} own={own} auto={actx.run_mode} '
+                  f'lse rel {rel(lv, ref_v[a:b]):.1e}', flush=True)
+    if n > 1:
+        assert mid, 'no case put a boundary inside a frame'
+    D.barrier()
+    D.shutdown()
+
+
+if __name__ == '__main__':
+    main()
