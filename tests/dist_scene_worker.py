@@ -4,8 +4,9 @@
 Every rank builds the same full tensors from a seeded CPU generator, keeps its partition's rows and runs the parallel
 path; the single-GPU result of the same layer is computed on every rank from the full tensors. Checks (the reference's
 tests/dist_onereel_kv_chunks.py, dist_onereel_overlap.py, dist_onereel_gather.py):
-  - K/V gathering (Hunyuan and Wan) equals the single-GPU result bit for bit (video rows and the text rows of the
-    scenes the rank touches), with halo and frame-memory frames, boundaries inside frames;
+  - K/V gathering (Hunyuan and Wan) equals the single-GPU result of the same key order bit for bit (video rows and
+    the text rows of the scenes the rank touches), with halo and frame-memory frames, boundaries inside frames; Wan's
+    one-GPU `ranges` reads the same keys in token order, so it is compared within rel 1e-2;
   - overlap='lse' (local keys during the exchange, LSE merge) within rel 1e-2 of waiting;
   - Ulysses equals the single-GPU result bit for bit; text_sync='all_reduce' equals 'rows' on touched scenes;
   - the Eq. 2 chooser ('auto') picks a path and reproduces the single-GPU result.
@@ -45,7 +46,9 @@ def main():
         D.world, D.rank = (lambda: 1), (lambda: 0)
         c1 = HY.Context(lay, T=T, own=[(0, L)], counts={True: counts}, fwd=1)
         ref_v, ref_t = HY.Processor(c1, 0).scene(q, k, v, eq, ek, ev)
-        wref = WN.Processor(WN.Context(lay, T=T, own=[(0, L)]), 'self', None, 0).ranges(q, k, v)
+        wproc1 = WN.Processor(WN.Context(lay, T=T, own=[(0, L)]), 'self', None, 0)
+        wref = wproc1.ranges(q, k, v)               # one GPU: contiguous key ranges in token order (or packed)
+        wref_scene = wproc1.scene(q, k, v)          # the gathering path's packed key order on one GPU
         D.world, D.rank = saved
         own = comm.partition(lay, n, T, 'scene', counts)
         a, b = own[r]
@@ -67,7 +70,8 @@ def main():
         assert rel(lv, ref_v[a:b]) < 1e-2 and rel(lt[trows], ref_t[trows]) < 1e-2, (lengths, r, 'lse')
         wc = WN.Context(lay, T=T, own=own)
         wv = WN.Processor(wc, 'self', None, 0).scene(ql, kl, vl)
-        assert torch.equal(wv, wref[a:b]), (lengths, r, 'wan video')
+        assert torch.equal(wv, wref_scene[a:b]), (lengths, r, 'wan video')
+        assert rel(wv, wref[a:b]) < 1e-2, (lengths, r, 'wan video vs ranges')   # same keys, another summation order
         # Ulysses: equal split, heads redistributed
         if L % n == 0 and H % n == 0:
             uown = comm.partition(lay, n, T, 'ulysses')
