@@ -58,6 +58,12 @@ struct AttnCfg {
 };
 
 constexpr int kThreads = 384;
+// of every 8 column pairs of a score row, how many evaluate 2^x with the FMA-pipe polynomial (ex2_fma) instead of
+// the MUFU ex2; the exponentials otherwise take as many MUFU clocks as the tile's MMAs take tensor clocks
+#ifndef ORL_EMU_PAIRS
+#define ORL_EMU_PAIRS 2
+#endif
+constexpr int kEmuPairs = ORL_EMU_PAIRS;
 
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* err) {
   const unsigned long long t0 = global_ns();
@@ -255,13 +261,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         float mx0 = __uint_as_float(r[0][0]), mx1 = __uint_as_float(r[1][0]);
         float mx2 = __uint_as_float(r[2][0]), mx3 = __uint_as_float(r[3][0]);
 #pragma unroll
-        for (int i = 1; i < 32; ++i) {
-          mx0 = fmaxf(mx0, __uint_as_float(r[0][i]));
-          mx1 = fmaxf(mx1, __uint_as_float(r[1][i]));
-          mx2 = fmaxf(mx2, __uint_as_float(r[2][i]));
-          mx3 = fmaxf(mx3, __uint_as_float(r[3][i]));
+        for (int i = 1; i < 31; i += 2) {
+          mx0 = fmax3(mx0, __uint_as_float(r[0][i]), __uint_as_float(r[0][i + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(r[1][i]), __uint_as_float(r[1][i + 1]));
+          mx2 = fmax3(mx2, __uint_as_float(r[2][i]), __uint_as_float(r[2][i + 1]));
+          mx3 = fmax3(mx3, __uint_as_float(r[3][i]), __uint_as_float(r[3][i + 1]));
         }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float mx = fmaxf(fmax3(mx0, mx1, __uint_as_float(r[0][31])),
+                               fmax3(mx2, mx3, fmax3(__uint_as_float(r[1][31]), __uint_as_float(r[2][31]),
+                                                     __uint_as_float(r[3][31]))));
         const float m_new = fmaxf(m_run, mx);
         const bool need = (m_new - m_run) * scale_log2 > 8.0f;
         const float m_use = need ? m_new : m_run;
@@ -275,8 +283,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) {
             const int c = 2 * h + (i >> 4);
             const int e = (2 * i) & 31;
-            const float p0 = ex2(fmaf(__uint_as_float(r[c][e]), scale_log2, neg));
-            const float p1 = ex2(fmaf(__uint_as_float(r[c][e + 1]), scale_log2, neg));
+            const float x0 = fmaf(__uint_as_float(r[c][e]), scale_log2, neg);
+            const float x1 = fmaf(__uint_as_float(r[c][e + 1]), scale_log2, neg);
+            // kEmuPairs of every 8 column pairs take 2^x on the FMA pipe, the rest on MUFU
+            const bool emu = (i & 7) < kEmuPairs;
+            const float p0 = emu ? ex2_fma(x0) : ex2(x0);
+            const float p1 = emu ? ex2_fma(x1) : ex2(x1);
             sum0 += p0;
             sum1 += p1;
             p[i] = pack_bf16x2(p0, p1);
