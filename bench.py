@@ -30,6 +30,11 @@ sys.path.insert(0, str(ROOT))
 CFG2 = dict(lengths=[8, 6, 10, 7], T=1590, text=128, heads=16, dim=128, memory=[0, 8, 14, 24])
 # a reduced cfg2 (first two scenes) for profiler captures: inputs still larger than L2, a few hundred MB on the device
 SMALL = dict(lengths=[8, 6], T=1590, text=128, heads=16, dim=128, memory=[0, 8])
+# BASELINE cfg3: Wan2.2-TI2V-5B-shaped layer through the joint [video | text] scene path, sharded (strong scaling)
+CFG3 = dict(lengths=[3, 12, 5, 9, 4, 8], T=880, text=256, heads=24, dim=128, memory=[0, 3, 15, 20])
+# BASELINE cfg4: full denoising step of the HunyuanVideo-1.5-architecture stand-in (4 scenes x 31 frames, 480p)
+CFG4 = dict(lengths=[31, 31, 31, 31], T=1590, text=128, heads=16, dim=128, memory=[0, 31, 62, 93], hidden=2048,
+            blocks=54, frame_hw=(30, 53))
 METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
 
 
@@ -153,11 +158,15 @@ def main():
     ap.add_argument('--mode', default='auto', choices=['auto', 'scene', 'ulysses'],
                     help='parallel path for N > 1 (auto = the Eq. 2 chooser)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small'],
-                    help='small: the first two scenes of cfg2, for profiler captures (not a bench line)')
+    ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small', 'cfg3', 'cfg4'],
+                    help='cfg2 (default bench line; weak scaling over N); small: the first two scenes of cfg2, for '
+                         'profiler captures; cfg3: BASELINE cfg3 layer sharded over N (strong scaling); cfg4: one '
+                         'full DiT denoising step of the stand-in (strong scaling)')
     args = ap.parse_args()
     if args.impl == 'reference':
         return run_reference(args)
+    if args.workload == 'cfg4':
+        return run_dit_step(args)
 
     from onereel_b200 import attention as A
     from onereel_b200 import dist as D
@@ -174,10 +183,11 @@ def main():
         build()                      # other ranks load the library rank 0 built
     dev = torch.device('cuda', local)
 
-    cfg = dict(CFG2 if args.workload == 'cfg2' else SMALL)
-    # weak scaling: N GPUs run cfg2's scene set repeated N times (per-GPU work fixed); every scene reads the frame
-    # memory of the first copy, so ranks exchange those rows (the path's real K/V gathering step)
-    cfg['lengths'] = cfg['lengths'] * world
+    cfg = dict({'cfg2': CFG2, 'small': SMALL, 'cfg3': CFG3}[args.workload])
+    if args.workload != 'cfg3':
+        # weak scaling: N GPUs run cfg2's scene set repeated N times (per-GPU work fixed); every scene reads the frame
+        # memory of the first copy, so ranks exchange those rows (the path's real K/V gathering step)
+        cfg['lengths'] = cfg['lengths'] * world
     lay = cfg_layout(cfg)
     T, H, Dh = cfg['T'], cfg['heads'], cfg['dim']
     counts = [cfg['text']] * lay.n_scenes
@@ -270,15 +280,16 @@ def main():
     h2d = sum(x.numel() * x.element_size() for x in host_in)
     d2h = sum(x.numel() * x.element_size() for x in host_out)
     line = dict(metric=METRIC, value=total_flops / (ms * 1e-3) / 1e12, unit='TFLOP/s', n_gpus=world,
-                steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling='weak',
+                steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True,
+                scaling='strong' if args.workload == 'cfg3' else 'weak',
                 vs_baseline=None, dtype='bf16', data='synthetic (seeded; Q/K RMS-normed N(0,1), V N(0,1))',
                 config=dict(workload=(f'{args.workload}: one HunyuanVideo-1.5-shaped scene-attention layer through '
                                       'hunyuan15.Processor.scene (pack K/V + attention' +
                                       (', K/V exchange over NCCL' if world > 1 else '') + ')'),
                             layout=dict(cfg, scenes=lay.n_scenes), run_mode=ctx.run_mode, path=ctx.path,
                             own=ctx.own, useful_tflop_per_step=total_flops / 1e12,
-                            parallelism=(f'scene-parallel x{world} (weak: cfg2 scene set repeated per GPU)'
-                                         if world > 1 else 'single'),
+                            parallelism=(f'{ctx.run_mode} x{world} ' + ('(strong: cfg3 fixed)' if args.workload == 'cfg3'
+                                         else '(weak: cfg2 scene set repeated per GPU)') if world > 1 else 'single'),
                             l2='inputs larger than L2 (q/k/v 203 MB each per GPU, packed K/V ~486 MB each)'),
                 e2e=dict(value=total_flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s', ms_per_step=e2e_ms,
                          h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
@@ -289,6 +300,73 @@ def main():
                               peak_source=f'{peak_kind} bf16 burst'),
                 gpu_launches=n_launches, clocks=clk.summary(), cpu_baseline=cb)
     print(json.dumps(line), flush=True)
+    D.shutdown()
+
+
+def run_dit_step(args):
+    """BASELINE cfg4: one denoising step (conditional + unconditional forward of 54 blocks) of the random-init
+    HunyuanVideo-1.5-architecture stand-in (onereel_b200/standin.py) on this rank's video rows, scene-parallel
+    attention through the B200 processors; latency = device time of the step, max over ranks (strong scaling)."""
+    from onereel_b200 import attention as A, dist as D, hunyuan15 as HY, standin
+    from onereel_b200.csrc.build import build
+    rank, world, local = dist_env()
+    if rank == 0:
+        build()
+    D.init('nccl')
+    if world > 1:
+        D.barrier()
+        build()
+    dev = torch.device('cuda', local)
+    cfg = CFG4
+    lay = cfg_layout(cfg)
+    T, H, Dh, C = cfg['T'], cfg['heads'], cfg['dim'], cfg['hidden']
+    counts = [cfg['text']] * lay.n_scenes
+    ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts})
+    HY.plan_parallel(ctx, H)
+    a, b = ctx.own[rank]
+    model = standin.build(ctx, dev, C, H, cfg['blocks'])
+    g = torch.Generator().manual_seed(1)
+    L, Nt = lay.n_frames * T, sum(counts)
+    hs = torch.randn(1, b - a, C, generator=g).to(dev, torch.bfloat16)
+    ehs_c, ehs_u = (torch.randn(1, Nt, C, generator=g).to(dev, torch.bfloat16) for _ in range(2))
+    temb = torch.randn(1, C, generator=g).to(dev, torch.bfloat16)
+    cos, sin = standin.rope_3d(lay.n_frames, *cfg['frame_hw'], Dh)
+    rot = (cos.to(dev), sin.to(dev))
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        standin.dit_step(model, ctx, hs, ehs_c, ehs_u, temb, rot)
+    torch.cuda.synchronize()
+    A.check()
+    with Clocks(local) as clk:
+        D.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            standin.dit_step(model, ctx, hs, ehs_c, ehs_u, temb, rot)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        D.barrier()
+    A.check()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    if rank == 0:
+        tokens = L + Nt
+        gemm = 2 * cfg['blocks'] * 24 * C * C * tokens
+        segs = [(s_.lq, s_.lk) for s_ in HY.S.scene_segments(lay, T, counts, [(j, (lo * T, hi * T)) for j, (lo, hi)
+                                                            in enumerate(lay.ranges)], set(range(lay.n_scenes)), (0, L))]
+        attn = 2 * cfg['blocks'] * sum(4.0 * x * y * H * Dh for x, y in segs)
+        print(json.dumps(dict(metric='DiT step latency (cfg4)', value=ms, unit='ms', n_gpus=world, steps=args.steps,
+                              warmup=args.warmup, ms_per_step=ms, higher_is_better=False, scaling='strong',
+                              dtype='bf16', data='synthetic (random-init stand-in, seeded)',
+                              config=dict(workload='cfg4: one denoising step (2 CFG forwards x 54 blocks) of the '
+                                                   'HunyuanVideo-1.5-architecture stand-in', layout=cfg,
+                                          run_mode=ctx.run_mode, path=ctx.path, own=ctx.own,
+                                          flop_per_step=dict(gemm=gemm, attention=attn)),
+                              achieved_tflops=(gemm + attn) / (ms * 1e-3) / 1e12, clocks=clk.summary())), flush=True)
     D.shutdown()
 
 

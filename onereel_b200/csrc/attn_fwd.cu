@@ -59,9 +59,10 @@ struct AttnCfg {
 
 constexpr int kThreads = 384;
 // of every 8 column pairs of a score row, how many evaluate 2^x with the FMA-pipe polynomial (ex2_fma) instead of
-// the MUFU ex2; the exponentials otherwise take as many MUFU clocks as the tile's MMAs take tensor clocks
+// the MUFU ex2. The exponentials take as many MUFU clocks as the tile's MMAs take tensor clocks, but measured on
+// cfg2 the extra FMA/ALU issue costs more than the MUFU time it saves, so the default keeps every ex2 on MUFU.
 #ifndef ORL_EMU_PAIRS
-#define ORL_EMU_PAIRS 2
+#define ORL_EMU_PAIRS 0
 #endif
 constexpr int kEmuPairs = ORL_EMU_PAIRS;
 
