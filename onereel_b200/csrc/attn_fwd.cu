@@ -7,12 +7,13 @@
 // One CTA computes one work item = (segment, head, up to 256 query rows as two 128-row tiles):
 //   warp 0      TMA producer: Q tiles once, then K_j / V_j tiles of 128 rows into a ring of shared-memory stages
 //   warp 1      TMEM owner and MMA issuer (one elected thread): S_t = Q_t K_j^T (SS form), O_t += P_t V_j (TS form,
-//               P read from TMEM), each group committed to an mbarrier
+//               P read from TMEM in two 64-key halves), each committed to an mbarrier
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: thread = query row = TMEM lane. Loads the S row,
-//               online max / exp2 / sum, writes P (bf16) over its S columns, rescales its O row in TMEM only when
-//               the running max grows by more than 2^8 (otherwise keeps the stale max: the result is identical and
-//               P stays <= 256), then normalises O and stores the bf16 row and its LSE.
+//               exponentiates against the running max while reducing the tile max (rescaling O in TMEM only when
+//               the max jumps by more than 2^64), writes P (bf16) over its S columns, then normalises O and stores
+//               the bf16 row and its LSE.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D,256+2D).
+// Warpgroup 0 runs on kRegsLow registers per thread and the softmax warpgroups on kRegsHigh (setmaxnreg).
 // Every mbarrier wait is bounded (ptx.cuh kWaitLimitNs): a stuck pipeline sets the error word and winds down.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -39,32 +40,33 @@ struct AttnCfg {
   static constexpr int kKOff = 2 * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_full, drain
+  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[t], p_full[t][half], all_done, drain
   static constexpr int kBarQ = 0;
   static constexpr int kBarK = 1;
   static constexpr int kBarV = kBarK + kStages;
   static constexpr int kBarE = kBarV + kStages;
-  static constexpr int kBarS = kBarE + kStages;
-  static constexpr int kBarP = kBarS + 2;
-  static constexpr int kBarO = kBarP + 2;
-  static constexpr int kBarDrain = kBarO + 1;
+  static constexpr int kBarS = kBarE + kStages;      // + t
+  static constexpr int kBarP = kBarS + 2;            // + 2 t + half
+  static constexpr int kBarDone = kBarP + 4;
+  static constexpr int kBarDrain = kBarDone + 1;
   static constexpr int kNumBars = kBarDrain + 1;
   static constexpr int kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = 512;
-  // TMEM column of S_t / O_t (t = 0, 1)
-  __host__ __device__ static constexpr uint32_t col_s(int t) { return t ? 128u : 0u; }
-  __host__ __device__ static constexpr uint32_t col_o(int t) { return t ? 256u + D : 256u; }
+  // TMEM columns: S of tile t (128 fp32 columns; its P is 64 bf16x2 columns at the same start), O of tile t
+  __host__ __device__ static constexpr uint32_t col_s(int t) { return 128u * t; }
+  __host__ __device__ static constexpr uint32_t col_o(int t) { return 256u + D * t; }
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 constexpr int kThreads = 384;
-// of every 8 column pairs of a score row, how many evaluate 2^x with the FMA-pipe polynomial (ex2_fma) instead of
-// the MUFU ex2. The exponentials take as many MUFU clocks as the tile's MMAs take tensor clocks, but measured on
-// cfg2 the extra FMA/ALU issue costs more than the MUFU time it saves, so the default keeps every ex2 on MUFU.
-#ifndef ORL_EMU_PAIRS
-#define ORL_EMU_PAIRS 0
-#endif
-constexpr int kEmuPairs = ORL_EMU_PAIRS;
+// register split: the launch has 384 threads x 168 registers; warpgroup 0 (producer, MMA issuer, two idle warps)
+// keeps kRegsLow, the two softmax warpgroups get kRegsHigh (4 x 32 x kRegsLow + 8 x 32 x kRegsHigh = 384 x 168)
+constexpr int kLaunchRegs = 168, kRegsLow = 88, kRegsHigh = 208;
+static_assert(4 * kRegsLow + 8 * kRegsHigh == 12 * kLaunchRegs, "register split must add up to the launch total");
+// The softmax exponentiates against the running max it already has and computes the tile's max alongside; only
+// when a score exceeds that max by more than 2^kMaxJump (in exp2 units) is the tile redone against the new max and
+// O rescaled. Below that, P <= 2^kMaxJump stays far inside bf16 / fp32 range and the final O / l is exact.
+constexpr float kMaxJump = 64.0f;
 
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* err) {
   const unsigned long long t0 = global_ns();
@@ -73,6 +75,274 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* e
       atomicOr(err, kErrTimeoutDrain);
       return;
     }
+  }
+}
+
+struct AttnShared {
+  uint32_t sbase;        // shared-window address of the 1024-aligned tile area
+  uint32_t bar0;         // address of barrier 0
+  volatile int* abort_flag;
+  __device__ uint32_t bar(int i) const { return bar0 + 8u * i; }
+};
+
+// ---------------------------------------------------------------------------------------------- TMA producer
+template <int D>
+__device__ __forceinline__ void producer_role(const AttnShared& sh, const CUtensorMap* tm_q, const CUtensorMap* tm_k,
+                                              const CUtensorMap* tm_v, const AttnWork& wi, int n_qt, int n_kv,
+                                              int* err) {
+  using C = AttnCfg<D>;
+  tma_prefetch_map(tm_q);
+  tma_prefetch_map(tm_k);
+  tma_prefetch_map(tm_v);
+  const uint64_t pol_q = policy_evict_first();
+  const uint64_t pol_kv = policy_evict_last();
+  const int x0 = wi.head * D;
+  mbar_expect_tx(sh.bar(C::kBarQ), n_qt * C::kTileBytes);
+  for (int t = 0; t < n_qt; ++t)
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_2d(sh.sbase + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, tm_q, sh.bar(C::kBarQ), x0 + 64 * c,
+                  wi.q_row0 + 128 * t, pol_q);
+  int issued = 0;
+  for (int j = 0; j < n_kv; ++j) {
+    const int s = j % C::kStages;
+    if (j >= C::kStages && !mbar_wait(sh.bar(C::kBarE + s), ((j / C::kStages) - 1) & 1, sh.abort_flag)) {
+      atomicOr(err, kErrTimeoutLoad);
+      break;
+    }
+    const int y = wi.k_row0 + 128 * j;
+    mbar_expect_tx(sh.bar(C::kBarK + s), C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_2d(sh.sbase + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, tm_k, sh.bar(C::kBarK + s),
+                  x0 + 64 * c, y, pol_kv);
+    mbar_expect_tx(sh.bar(C::kBarV + s), C::kTileBytes);
+    for (int c = 0; c < C::kChunks; ++c)
+      tma_load_2d(sh.sbase + C::kVOff + s * C::kTileBytes + c * C::kChunkBytes, tm_v, sh.bar(C::kBarV + s),
+                  x0 + 64 * c, y, pol_kv);
+    issued = j + 1;
+  }
+  if (*sh.abort_flag) {
+    // wind down: every copy this thread started must land before the CTA's shared memory is released
+    drain_wait(sh.bar(C::kBarQ), 0, err);
+    for (int j = issued > C::kStages ? issued - C::kStages : 0; j < issued; ++j) {
+      const int s = j % C::kStages;
+      drain_wait(sh.bar(C::kBarK + s), (j / C::kStages) & 1, err);
+      drain_wait(sh.bar(C::kBarV + s), (j / C::kStages) & 1, err);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- MMA issuer
+// Per 128-key tile j: S_t = Q_t K_j^T (both operands from shared memory) and O_t += P_t V_j (A = P from TMEM,
+// B = V MN-major), P handed over in two 64-key halves so the PV of the first half starts while the softmax warps
+// still exponentiate the second. Issue order: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1): the tensor pipe computes one
+// tile while the softmax warps work on the other.
+template <int D>
+__device__ __forceinline__ void mma_role(const AttnShared& sh, uint32_t tmem, int n_qt, int n_kv, int* err) {
+  using C = AttnCfg<D>;
+  constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
+  constexpr uint32_t kIdescO = idesc_bf16(128, D, false, true);
+  auto issue_s = [&](int t, int s) {
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t off = (kk >> 2) * C::kChunkBytes + (kk & 3) * 32;
+      const uint64_t a = smem_desc_sw128(sh.sbase + C::kQOff + t * C::kTileBytes + off, 16, 1024);
+      const uint64_t b = smem_desc_sw128(sh.sbase + C::kKOff + s * C::kTileBytes + off, 16, 1024);
+      mma_ss(tmem + C::col_s(t), a, b, kIdescS, kk > 0 ? 1u : 0u);
+    }
+  };
+  auto issue_o = [&](int t, int half, int s, bool acc) {
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+      const int kk = 4 * half + k4;
+      const uint64_t b = smem_desc_sw128(sh.sbase + C::kVOff + s * C::kTileBytes + kk * 2048, C::kChunkBytes, 1024);
+      mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, b, kIdescO, (acc || kk > 0) ? 1u : 0u);
+    }
+  };
+  bool ok = mbar_wait(sh.bar(C::kBarQ), 0, sh.abort_flag) && mbar_wait(sh.bar(C::kBarK), 0, sh.abort_flag);
+  if (ok) {
+    for (int t = 0; t < n_qt; ++t) {
+      issue_s(t, 0);
+      mma_commit(sh.bar(C::kBarS + t));
+    }
+  }
+  for (int j = 0; ok && j < n_kv; ++j) {
+    const int s = j % C::kStages;
+    const int s2 = (j + 1) % C::kStages;
+    const bool more = j + 1 < n_kv;
+    bool k_next = false;                 // K of tile j + 1 waited for (lazily, before its first S)
+    ok = mbar_wait(sh.bar(C::kBarV + s), (j / C::kStages) & 1, sh.abort_flag);
+    for (int t = 0; ok && t < n_qt; ++t) {
+      for (int half = 0; ok && half < 2; ++half) {
+        ok = mbar_wait(sh.bar(C::kBarP + 2 * t + half), j & 1, sh.abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        issue_o(t, half, s, j > 0);
+      }
+      if (!ok) break;
+      if (t == n_qt - 1) mma_commit(sh.bar(C::kBarE + s));
+      if (more) {
+        if (!k_next) {
+          ok = mbar_wait(sh.bar(C::kBarK + s2), ((j + 1) / C::kStages) & 1, sh.abort_flag);
+          if (!ok) break;
+          k_next = true;
+        }
+        issue_s(t, s2);
+        mma_commit(sh.bar(C::kBarS + t));
+      }
+    }
+  }
+  if (ok) {
+    mma_commit(sh.bar(C::kBarDone));
+  } else {
+    atomicOr(err, kErrTimeoutMma);
+    mma_commit(sh.bar(C::kBarDrain));
+    drain_wait(sh.bar(C::kBarDrain), 0, err);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- softmax
+// One thread per query row (= TMEM lane) of tile t. Per 128-key tile: load the S row, mask keys past the segment,
+// exponentiate against the running max while reducing the tile's max alongside (the first tile takes its max first);
+// if the tile's max exceeds the running one by more than kMaxJump (exp2 units) the warp redoes the tile against the
+// new max and rescales its O rows in TMEM (PV of the previous tile has completed: S of this tile was issued after
+// it). P (bf16) goes over the S columns in two halves, each handed to the MMA warp as soon as it is stored.
+template <int D>
+__device__ __forceinline__ void softmax_role(const AttnShared& sh, uint32_t tmem, int t, int quad, int lane,
+                                             const AttnWork& wi, int n_kv, float scale_log2,
+                                             __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
+                                             long long nq_total, int heads, int* err) {
+  using C = AttnCfg<D>;
+  const int row = 32 * quad + lane;
+  const int item_row = 128 * t + row;
+  const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
+  const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
+  const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
+  const bool row_valid = item_row < wi.q_len;
+  __nv_bfloat16* orow = out + (static_cast<long long>(wi.q_row0) + item_row) * heads * D + wi.head * D;
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = n_kv > 0;
+  for (int j = 0; ok && j < n_kv; ++j) {
+    ok = mbar_wait(sh.bar(C::kBarS + t), j & 1, sh.abort_flag);
+    if (!ok) break;
+    tc_fence_after();
+    uint32_t r[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, r[c]);
+    tmem_wait_ld();
+    const int valid = wi.k_len - 128 * j;
+    if (valid < 128) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (32 * c + e >= valid) r[c][e] = __float_as_uint(-INFINITY);
+    }
+    auto row_max = [&]() {
+      float m0 = __uint_as_float(r[0][0]), m1 = __uint_as_float(r[1][0]);
+      float m2 = __uint_as_float(r[2][0]), m3 = __uint_as_float(r[3][0]);
+#pragma unroll
+      for (int e = 1; e < 31; e += 2) {
+        m0 = fmax3(m0, __uint_as_float(r[0][e]), __uint_as_float(r[0][e + 1]));
+        m1 = fmax3(m1, __uint_as_float(r[1][e]), __uint_as_float(r[1][e + 1]));
+        m2 = fmax3(m2, __uint_as_float(r[2][e]), __uint_as_float(r[2][e + 1]));
+        m3 = fmax3(m3, __uint_as_float(r[3][e]), __uint_as_float(r[3][e + 1]));
+      }
+      return fmaxf(fmax3(m0, m1, __uint_as_float(r[0][31])),
+                   fmax3(m2, m3, fmax3(__uint_as_float(r[1][31]), __uint_as_float(r[2][31]),
+                                       __uint_as_float(r[3][31]))));
+    };
+    // exponentials of columns [64 half, 64 half + 64) against -m * log2e * scale = neg: packed bf16 P, sum
+    auto exp_half = [&](int half, float neg, uint32_t (&p)[32]) {
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int c = 2 * half + (e >> 4);
+        const int k = (2 * e) & 31;
+        const float p0 = ex2(fmaf(__uint_as_float(r[c][k]), scale_log2, neg));
+        const float p1 = ex2(fmaf(__uint_as_float(r[c][k + 1]), scale_log2, neg));
+        if (e & 1) {
+          s2 += p0;
+          s3 += p1;
+        } else {
+          s0 += p0;
+          s1 += p1;
+        }
+        p[e] = pack_bf16x2(p0, p1);
+      }
+      return (s0 + s1) + (s2 + s3);
+    };
+    float m_use = m_run;
+    bool redo = false;
+    uint32_t pa[32];
+    float sum;
+    if (j == 0) {
+      m_use = row_max();
+      sum = exp_half(0, -m_use * scale_log2, pa);
+    } else {
+      sum = exp_half(0, -m_run * scale_log2, pa);       // speculative: the max is reduced alongside
+      const float mx = row_max();
+      redo = (mx - m_run) * scale_log2 > kMaxJump;
+      if (__any_sync(0xffffffffu, redo)) {
+        m_use = fmaxf(m_run, mx);
+        const float alpha = ex2((m_run - m_use) * scale_log2);
+        sum = exp_half(0, -m_use * scale_log2, pa);
+        l_run *= alpha;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_addr + 32 * c, o);
+        }
+      }
+    }
+    tmem_st32(s_addr, pa);
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(sh.bar(C::kBarP + 2 * t + 0));
+    uint32_t pb[32];
+    sum += exp_half(1, -m_use * scale_log2, pb);
+    tmem_st32(s_addr + 32, pb);
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(sh.bar(C::kBarP + 2 * t + 1));
+    l_run += sum;
+    m_run = m_use;
+  }
+  if (ok) ok = mbar_wait(sh.bar(C::kBarDone), 0, sh.abort_flag);
+  if (ok) {
+    tc_fence_after();
+    const float inv = 1.0f / l_run;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32(o_addr + 32 * c, o);
+      tmem_wait_ld();
+      if (row_valid) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+          dst[v] = w;
+        }
+      }
+    }
+    if (lse != nullptr && row_valid)
+      lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] =
+          (m_run * scale_log2 + lg2(l_run)) * 0.69314718055994530942f;
+  } else if (n_kv > 0) {
+    atomicOr(err, kErrTimeoutSoftmax);
+  } else if (row_valid) {
+    // a segment without keys: zero output, LSE -inf
+    uint4* dst = reinterpret_cast<uint4*>(orow);
+    for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+    if (lse != nullptr) lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] = -INFINITY;
   }
 }
 
@@ -85,10 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = AttnCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOff + C::kNumBars * 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  auto bar = [&](int i) -> uint32_t { return sbase + C::kBarOff + 8u * i; };
+  AttnShared sh;
+  sh.sbase = smem_u32(smem);
+  sh.bar0 = sh.sbase + C::kBarOff;
+  sh.abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -97,19 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv = (wi.k_len + 127) >> 7;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(C::kBarQ), 1);
+    mbar_init(sh.bar(C::kBarQ), 1);
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(bar(C::kBarK + s), 1);
-      mbar_init(bar(C::kBarV + s), 1);
-      mbar_init(bar(C::kBarE + s), 1);
+      mbar_init(sh.bar(C::kBarK + s), 1);
+      mbar_init(sh.bar(C::kBarV + s), 1);
+      mbar_init(sh.bar(C::kBarE + s), 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(C::kBarS + t), 1);
-      mbar_init(bar(C::kBarP + t), 128);
-    }
-    mbar_init(bar(C::kBarO), 1);
-    mbar_init(bar(C::kBarDrain), 1);
-    *abort_flag = 0;
+    for (int t = 0; t < 2; ++t) mbar_init(sh.bar(C::kBarS + t), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(sh.bar(C::kBarP + i), 128);
+    mbar_init(sh.bar(C::kBarDone), 1);
+    mbar_init(sh.bar(C::kBarDrain), 1);
+    *sh.abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -121,232 +390,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (elect_one() && n_kv > 0) {
-      tma_prefetch_map(&tm_q);
-      tma_prefetch_map(&tm_k);
-      tma_prefetch_map(&tm_v);
-      const uint64_t pol_q = policy_evict_first();
-      const uint64_t pol_kv = policy_evict_last();
-      const int x0 = wi.head * D;
-      mbar_expect_tx(bar(C::kBarQ), n_qt * C::kTileBytes);
-      for (int t = 0; t < n_qt; ++t)
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_2d(sbase + C::kQOff + t * C::kTileBytes + c * C::kChunkBytes, &tm_q, bar(C::kBarQ), x0 + 64 * c,
-                      wi.q_row0 + 128 * t, pol_q);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % C::kStages;
-        if (j >= C::kStages && !mbar_wait(bar(C::kBarE + s), ((j / C::kStages) - 1) & 1, abort_flag)) {
-          atomicOr(err, kErrTimeoutLoad);
-          break;
-        }
-        const int y = wi.k_row0 + 128 * j;
-        mbar_expect_tx(bar(C::kBarK + s), C::kTileBytes);
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_2d(sbase + C::kKOff + s * C::kTileBytes + c * C::kChunkBytes, &tm_k, bar(C::kBarK + s),
-                      x0 + 64 * c, y, pol_kv);
-        mbar_expect_tx(bar(C::kBarV + s), C::kTileBytes);
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_2d(sbase + C::kVOff + s * C::kTileBytes + c * C::kChunkBytes, &tm_v, bar(C::kBarV + s),
-                      x0 + 64 * c, y, pol_kv);
-        issued = j + 1;
-      }
-      if (*abort_flag) {
-        // wind down: every copy this thread started must land before the CTA's shared memory is released
-        drain_wait(bar(C::kBarQ), 0, err);
-        for (int j = std::max(0, issued - C::kStages); j < issued; ++j) {
-          const int s = j % C::kStages;
-          drain_wait(bar(C::kBarK + s), (j / C::kStages) & 1, err);
-          drain_wait(bar(C::kBarV + s), (j / C::kStages) & 1, err);
-        }
-      }
+  if (warp < 4) {
+    // warpgroup 0 returns registers at one program point (all four warps), then splits into its roles
+    regs_dec<kRegsLow>();
+    if (warp == 0) {
+      if (elect_one() && n_kv > 0) producer_role<D>(sh, &tm_q, &tm_k, &tm_v, wi, n_qt, n_kv, err);
+    } else if (warp == 1) {
+      if (elect_one() && n_kv > 0) mma_role<D>(sh, tmem, n_qt, n_kv, err);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (elect_one() && n_kv > 0) {
-      constexpr uint32_t kIdescS = idesc_bf16(128, 128, false, false);
-      constexpr uint32_t kIdescO = idesc_bf16(128, D, false, true);
-      bool ok = mbar_wait(bar(C::kBarQ), 0, abort_flag);
-      auto issue_s = [&](int t, int s) {
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::kChunkBytes + (kk & 3) * 32;
-          const uint64_t a = smem_desc_sw128(sbase + C::kQOff + t * C::kTileBytes + off, 16, 1024);
-          const uint64_t b = smem_desc_sw128(sbase + C::kKOff + s * C::kTileBytes + off, 16, 1024);
-          mma_ss(tmem + C::col_s(t), a, b, kIdescS, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_o = [&](int t, int s, bool acc) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t b = smem_desc_sw128(sbase + C::kVOff + s * C::kTileBytes + kk * 2048, C::kChunkBytes, 1024);
-          mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, b, kIdescO, (acc || kk > 0) ? 1u : 0u);
-        }
-      };
-      if (ok) ok = mbar_wait(bar(C::kBarK + 0), 0, abort_flag);
-      if (ok) {
-        issue_s(0, 0);
-        mma_commit(bar(C::kBarS + 0));
-        if (n_qt == 2) {
-          issue_s(1, 0);
-          mma_commit(bar(C::kBarS + 1));
-        }
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j % C::kStages;
-        const int s2 = (j + 1) % C::kStages;
-        const bool more = j + 1 < n_kv;
-        ok = mbar_wait(bar(C::kBarV + s), (j / C::kStages) & 1, abort_flag) &&
-             mbar_wait(bar(C::kBarP + 0), j & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        issue_o(0, s, j > 0);
-        if (more) {
-          ok = mbar_wait(bar(C::kBarK + s2), ((j + 1) / C::kStages) & 1, abort_flag);
-          if (!ok) break;
-          issue_s(0, s2);
-          mma_commit(bar(C::kBarS + 0));
-        }
-        if (n_qt == 2) {
-          ok = mbar_wait(bar(C::kBarP + 1), j & 1, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          issue_o(1, s, j > 0);
-        }
-        mma_commit(bar(C::kBarE + s));
-        if (n_qt == 2 && more) {
-          issue_s(1, s2);
-          mma_commit(bar(C::kBarS + 1));
-        }
-      }
-      if (ok) {
-        mma_commit(bar(C::kBarO));
-      } else {
-        atomicOr(err, kErrTimeoutMma);
-        mma_commit(bar(C::kBarDrain));
-        drain_wait(bar(C::kBarDrain), 0, err);
-      }
-    }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax / correction / epilogue
+  } else {
+    regs_inc<kRegsHigh>();
     const int t = (warp - 4) >> 2;
-    const int quad = warp & 3;
-    const int row = 32 * quad + lane;                 // row within tile t = TMEM lane
-    const int item_row = 128 * t + row;
-    const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
-    const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
-    const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
-    const bool row_valid = item_row < wi.q_len;
-    __nv_bfloat16* orow = out + (static_cast<long long>(wi.q_row0) + item_row) * heads * D + wi.head * D;
-    if (t < n_qt) {
-      float m_run = -INFINITY, l_run = 0.f;
-      bool ok = n_kv > 0;
-      for (int j = 0; ok && j < n_kv; ++j) {
-        ok = mbar_wait(bar(C::kBarS + t), j & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t r[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, r[c]);
-        tmem_wait_ld();
-        const int valid = wi.k_len - 128 * j;
-        if (valid < 128) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (32 * c + i >= valid) r[c][i] = __float_as_uint(-INFINITY);
-        }
-        float mx0 = __uint_as_float(r[0][0]), mx1 = __uint_as_float(r[1][0]);
-        float mx2 = __uint_as_float(r[2][0]), mx3 = __uint_as_float(r[3][0]);
-#pragma unroll
-        for (int i = 1; i < 31; i += 2) {
-          mx0 = fmax3(mx0, __uint_as_float(r[0][i]), __uint_as_float(r[0][i + 1]));
-          mx1 = fmax3(mx1, __uint_as_float(r[1][i]), __uint_as_float(r[1][i + 1]));
-          mx2 = fmax3(mx2, __uint_as_float(r[2][i]), __uint_as_float(r[2][i + 1]));
-          mx3 = fmax3(mx3, __uint_as_float(r[3][i]), __uint_as_float(r[3][i + 1]));
-        }
-        const float mx = fmaxf(fmax3(mx0, mx1, __uint_as_float(r[0][31])),
-                               fmax3(mx2, mx3, fmax3(__uint_as_float(r[1][31]), __uint_as_float(r[2][31]),
-                                                     __uint_as_float(r[3][31]))));
-        const float m_new = fmaxf(m_run, mx);
-        const bool need = (m_new - m_run) * scale_log2 > 8.0f;
-        const float m_use = need ? m_new : m_run;
-        const float alpha = ex2((m_run - m_use) * scale_log2);
-        const float neg = -m_use * scale_log2;
-        float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t p[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = 2 * h + (i >> 4);
-            const int e = (2 * i) & 31;
-            const float x0 = fmaf(__uint_as_float(r[c][e]), scale_log2, neg);
-            const float x1 = fmaf(__uint_as_float(r[c][e + 1]), scale_log2, neg);
-            // kEmuPairs of every 8 column pairs take 2^x on the FMA pipe, the rest on MUFU
-            const bool emu = (i & 7) < kEmuPairs;
-            const float p0 = emu ? ex2_fma(x0) : ex2(x0);
-            const float p1 = emu ? ex2_fma(x1) : ex2(x1);
-            sum0 += p0;
-            sum1 += p1;
-            p[i] = pack_bf16x2(p0, p1);
-          }
-          tmem_st32(s_addr + 32 * h, p);
-        }
-        l_run = l_run * alpha + (sum0 + sum1);
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(o_addr + 32 * c, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(o_addr + 32 * c, o);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(C::kBarP + t));
-        m_run = m_use;
-      }
-      if (ok) ok = mbar_wait(bar(C::kBarO), 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        const float inv = 1.0f / l_run;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + 32 * c, o);
-          tmem_wait_ld();
-          if (row_valid) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-              dst[v] = w;
-            }
-          }
-        }
-        if (lse != nullptr && row_valid)
-          lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] =
-              (m_run * scale_log2 + lg2(l_run)) * 0.69314718055994530942f;
-      } else if (n_kv > 0) {
-        atomicOr(err, kErrTimeoutSoftmax);
-      } else if (row_valid) {
-        // a segment without keys: zero output, LSE -inf
-        uint4* dst = reinterpret_cast<uint4*>(orow);
-        for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
-        if (lse != nullptr) lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] = -INFINITY;
-      }
-    }
+    if (t < n_qt) softmax_role<D>(sh, tmem, t, warp & 3, lane, wi, n_kv, scale_log2, out, lse, nq_total, heads, err);
   }
 
   tc_fence_before();

@@ -211,31 +211,24 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Per-warp register budget change (warpgroup-wide: every warp of the warpgroup executes it). The launch's
+// registers (threads x registers per thread) are redistributed: decreases return registers to the pool, increases
+// wait until the pool has them, so the split must add up to the launch total.
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------------------------------------------ math
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA pipe (offloads the MUFU unit), for x <= 126. x is split as n + f with n = round(x) by the
-// 1.5 * 2^23 shift (the sum's low mantissa bits are n), f in [-1/2, 1/2]; 2^f is a degree-3 polynomial and n is
-// added to its exponent field. The coefficients are a near-minimax relative-error fit of 2^f on [-1/2, 1/2] made for
-// this kernel (least squares reweighted by Lawson's algorithm toward the minimax solution): max relative error
-// 7.5e-5, far below the bf16 spacing (2^-8) of the P values it feeds. Inputs below -125 are clamped there (2^-125
-// is below every bf16 P that matters and keeps the exponent field normal).
-__device__ __forceinline__ float ex2_fma(float x) {
-  constexpr float kShift = 12582912.0f;                    // 1.5 * 2^23
-  float t, r, f;
-  x = fmaxf(x, -125.0f);
-  asm("add.rn.f32 %0, %1, %2;" : "=f"(t) : "f"(x), "f"(kShift));
-  asm("sub.rn.f32 %0, %1, %2;" : "=f"(r) : "f"(t), "f"(kShift));
-  asm("sub.rn.f32 %0, %1, %2;" : "=f"(f) : "f"(x), "f"(r));
-  float p = fmaf(0.05517134442925453f, f, 0.24261033535003662f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999281167984009f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // max of three floats in one instruction (sm_100)
