@@ -155,8 +155,9 @@ def main():
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--mode', default='auto', choices=['auto', 'scene', 'ulysses'],
-                    help='parallel path for N > 1 (auto = the Eq. 2 chooser)')
+    ap.add_argument('--mode', default='auto',
+                    help='parallel path for N > 1: auto (the Eq. 2 chooser), scene or ulysses; a comma list runs '
+                         'each in turn and prints one line per mode')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small', 'cfg3', 'cfg4'],
                     help='cfg2 (default bench line; weak scaling over N); small: the first two scenes of cfg2, for '
@@ -167,7 +168,14 @@ def main():
         return run_reference(args)
     if args.workload == 'cfg4':
         return run_dit_step(args)
+    modes = args.mode.split(',')
+    for i, mode in enumerate(modes):
+        args.mode = mode
+        run_layer(args, last=i == len(modes) - 1)
 
+
+def run_layer(args, last=True):
+    """one scene-attention layer per step through the public processor API (the default bench line)"""
     from onereel_b200 import attention as A
     from onereel_b200 import dist as D
     from onereel_b200 import hunyuan15 as HY
@@ -270,7 +278,8 @@ def main():
         dist.all_reduce(f)
         total_flops = f.item()
     if rank != 0:
-        D.shutdown()
+        if last:
+            D.shutdown()
         return
     peak_burst, peak_sus, hbm, peak_kind = peaks()
     achieved = rank_flops / (attn_ms * 1e-3) / 1e12
@@ -300,7 +309,8 @@ def main():
                               peak_source=f'{peak_kind} bf16 burst'),
                 gpu_launches=n_launches, clocks=clk.summary(), cpu_baseline=cb)
     print(json.dumps(line), flush=True)
-    D.shutdown()
+    if last:
+        D.shutdown()
 
 
 def run_dit_step(args):

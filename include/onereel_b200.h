@@ -122,6 +122,16 @@ ORL_API int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_v
 ORL_API int orl_lse_merge(void* o1, float* lse1, const void* o2, const float* lse2, long long n, long long ld_lse1,
                   long long ld_lse2, int heads, int head_dim, void* stream);
 
+/* Fused q/k RMSNorm + rotary embedding (the q/k preparation of hunyuan15.py:187-190 and wan.py:64-74 `_qk`, which
+ * the reference runs as separate ops / a torch.compile'd Triton kernel): x, y [rows, heads * head_dim] bf16 (y may
+ * alias x); weight bf16 [head_dim] (per_head = 1: RMSNorm over each head, Hunyuan) or [heads * head_dim] (per_head =
+ * 0: over the whole row, Wan); cos_t / sin_t fp32 [rows, rope_ld], pair i of a head rotated by cos[2i] and
+ * sin[2i + sin_shift] (sin_shift 0: tables repeated per pair, Hunyuan; 1: Wan's cos[..., 0::2] / sin[..., 1::2]).
+ * row_map (optional): output row of each input row (write straight into a packed layout). */
+ORL_API int orl_qk_norm_rope(const void* x, void* y, const void* weight, const float* cos_t, const float* sin_t,
+                             long long rows, int heads, int head_dim, int per_head, float eps, int sin_shift,
+                             long long rope_ld, const int32_t* row_map, void* stream);
+
 /* ---------------------------------------------------------------- native planner (comm.py:18-112, layout.py:54-78) */
 
 /* A scene layout (layout.py:10-18 SceneLayout): lengths[n_scenes] latent frames per scene, halo frames of the

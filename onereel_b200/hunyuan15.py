@@ -21,6 +21,7 @@ from onereel_b200 import attention as A
 from onereel_b200 import comm, dist as D
 from onereel_b200 import scene as S
 from onereel_b200.layout import SceneLayout
+from onereel_b200.rope import qk_norm_rope
 
 
 @dataclass
@@ -130,12 +131,13 @@ class Processor:
         cos, sin = image_rotary_emb
         ctx._rot_full = image_rotary_emb
         a, b = ctx.own[D.rank()]
-        rot = (cos[a:b], sin[a:b])
-        q, k, v = (f(hidden_states).unflatten(2, (attn.heads, -1)) for f in (attn.to_q, attn.to_k, attn.to_v))
-        q, k = attn.norm_q(q), attn.norm_k(k)
-        q = apply_rotary_emb(q, rot)[0].to(torch.bfloat16).contiguous()
-        k = apply_rotary_emb(k, rot)[0].to(torch.bfloat16).contiguous()
-        v = v[0].to(torch.bfloat16).contiguous()
+        H = attn.heads
+        # per-head RMSNorm + rotary embedding of the local rows in one fused kernel (orl_qk_norm_rope)
+        q = qk_norm_rope(attn.to_q(hidden_states).to(torch.bfloat16), attn.norm_q.weight, cos[a:b], sin[a:b], H,
+                         attn.norm_q.eps, per_head=True, sin_shift=0)
+        k = qk_norm_rope(attn.to_k(hidden_states).to(torch.bfloat16), attn.norm_k.weight, cos[a:b], sin[a:b], H,
+                         attn.norm_k.eps, per_head=True, sin_shift=0)
+        v = attn.to_v(hidden_states).unflatten(2, (H, -1))[0].to(torch.bfloat16).contiguous()
         eq, ek, ev = (f(encoder_hidden_states).unflatten(2, (attn.heads, -1))
                       for f in (attn.add_q_proj, attn.add_k_proj, attn.add_v_proj))
         if getattr(attn, 'norm_added_q', None) is not None:
@@ -246,7 +248,8 @@ class Processor:
 
 def apply_rotary_emb(x, freqs):
     """real-valued rotary embedding over interleaved pairs (diffusers' apply_rotary_emb with use_real=True,
-    use_real_unbind_dim=-1, sequence_dim=1): x [B, S, H, D], cos / sin [S, D]"""
+    use_real_unbind_dim=-1, sequence_dim=1): x [B, S, H, D], cos / sin [S, D]. Torch ops; the processor uses the fused
+    orl_qk_norm_rope kernel, this stays for callers that rotate other tensors."""
     cos, sin = (f[None, :, None, :].to(x.device) for f in freqs)
     xr, xi = x.float().unflatten(-1, (-1, 2)).unbind(-1)
     rot = torch.stack([-xi, xr], -1).flatten(-2)

@@ -18,6 +18,7 @@ from onereel_b200 import comm, dist as D
 from onereel_b200 import scene as S
 from onereel_b200.hunyuan15 import _attend, _layout_key
 from onereel_b200.layout import SceneLayout
+from onereel_b200.rope import qk_norm_rope as fused_qk_norm_rope
 
 TEXT_LEN = 512
 
@@ -52,7 +53,8 @@ class Context:
 
 
 def qk_norm_rope(q, k, wq, wk, eps: float, cos, sin, heads: int):
-    """wan.py:64-74: RMSNorm over the hidden dimension, then the interleaved RoPE of diffusers' Wan attention"""
+    """wan.py:64-74 in torch ops: RMSNorm over the hidden dimension, then the interleaved RoPE of diffusers' Wan
+    attention. The processor uses the fused orl_qk_norm_rope kernel; this is the same math for other callers."""
     def norm(x, w):
         return F.rms_norm(x, (x.shape[-1],), w, eps)
 
@@ -80,11 +82,14 @@ class Processor:
             return torch.cat([self.orig(attn, hidden_states[:, lo:hi],
                                         encoder_hidden_states[:, j * TEXT_LEN:(j + 1) * TEXT_LEN], None, rotary_emb)
                               for j, lo, hi in pieces], 1)
-        cos, sin = (x[:, a:b] for x in rotary_emb)
-        q, k, v = attn.to_q(hidden_states), attn.to_k(hidden_states), attn.to_v(hidden_states)
-        q, k = qk_norm_rope(q, k, attn.norm_q.weight, attn.norm_k.weight, attn.norm_q.eps, cos, sin, attn.heads)
-        v = v.unflatten(2, (attn.heads, -1))
-        q, k, v = (x[0].to(torch.bfloat16).contiguous() for x in (q, k, v))
+        cos, sin = (x[:, a:b].reshape(b - a, -1) for x in rotary_emb)
+        H = attn.heads
+        # hidden-dimension RMSNorm + Wan's interleaved RoPE in one fused kernel (replaces the compiled _qk)
+        q = fused_qk_norm_rope(attn.to_q(hidden_states).to(torch.bfloat16), attn.norm_q.weight, cos, sin, H,
+                               attn.norm_q.eps, per_head=False, sin_shift=1)
+        k = fused_qk_norm_rope(attn.to_k(hidden_states).to(torch.bfloat16), attn.norm_k.weight, cos, sin, H,
+                               attn.norm_k.eps, per_head=False, sin_shift=1)
+        v = attn.to_v(hidden_states).unflatten(2, (H, -1))[0].to(torch.bfloat16).contiguous()
         if ctx.attn_override is not None:
             qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
             r = ctx.attn_override(self.layer, qa, ka, va)
