@@ -122,6 +122,11 @@ ORL_API int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_v
 ORL_API int orl_lse_merge(void* o1, float* lse1, const void* o2, const float* lse2, long long n, long long ld_lse1,
                   long long ld_lse2, int heads, int head_dim, void* stream);
 
+/* As orl_lse_merge with an fp32 accumulator (parallel/ring.py:63-70 `_merge`, which keeps o in fp32 across the ring
+ * steps): acc [n, heads, head_dim] fp32 and lse_acc [heads, ld_lse1] (in/out) merged with a bf16 part and its lse. */
+ORL_API int orl_lse_merge_acc(float* acc, float* lse_acc, const void* part, const float* lse_part, long long n,
+                              long long ld_lse1, long long ld_lse2, int heads, int head_dim, void* stream);
+
 /* Fused q/k RMSNorm + rotary embedding (the q/k preparation of hunyuan15.py:187-190 and wan.py:64-74 `_qk`, which
  * the reference runs as separate ops / a torch.compile'd Triton kernel): x, y [rows, heads * head_dim] bf16 (y may
  * alias x); weight bf16 [head_dim] (per_head = 1: RMSNorm over each head, Hunyuan) or [heads * head_dim] (per_head =

@@ -199,3 +199,13 @@ def lse_merge(o1, lse1, o2, lse2):
     L.check(L.lib().orl_lse_merge(o1.data_ptr(), lse1.data_ptr(), o2.data_ptr(), lse2.data_ptr(), n, lse1.stride(0),
                                   lse2.stride(0), H, Dh, s), 'orl_lse_merge')
     return o1, lse1
+
+
+def lse_merge_acc(acc, lse_acc, part, lse_part):
+    """in place: fp32 (acc, lse_acc) <- merged with a bf16 partial result (part, lse_part) over disjoint keys
+    (ring.py:63-70). acc [n, H, D] fp32 / part [n, H, D] bf16 contiguous rows, lse [H, >= n] fp32."""
+    n, H, Dh = acc.shape
+    s = torch.cuda.current_stream(acc.device).cuda_stream
+    L.check(L.lib().orl_lse_merge_acc(acc.data_ptr(), lse_acc.data_ptr(), part.data_ptr(), lse_part.data_ptr(), n,
+                                      lse_acc.stride(0), lse_part.stride(0), H, Dh, s), 'orl_lse_merge_acc')
+    return acc, lse_acc

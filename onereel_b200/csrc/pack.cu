@@ -113,6 +113,30 @@ __global__ void lse_merge_kernel(__nv_bfloat16* __restrict__ o1, float* __restri
   if (lane == 0) lse1[h * ld1 + row] = m + __logf(den);
 }
 
+// fp32 accumulator version (parallel/ring.py:63-70 `_merge`): acc (fp32, in/out) with lse_acc merged with a bf16
+// partial result and its lse.
+__global__ void lse_merge_acc_kernel(float* __restrict__ acc, float* __restrict__ lse_acc,
+                                     const __nv_bfloat16* __restrict__ part, const float* __restrict__ lse_part,
+                                     long long n, long long ld1, long long ld2, int heads, int head_dim) {
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= n * heads) return;
+  const long long row = wid / heads;
+  const int h = static_cast<int>(wid - row * heads);
+  const float l1 = lse_acc[h * ld1 + row], l2 = lse_part[h * ld2 + row];
+  float m = fmaxf(l1, l2);
+  if (isinf(m)) m = 0.f;
+  const float w1 = __expf(l1 - m), w2 = __expf(l2 - m);
+  const float den = w1 + w2;
+  const float a = w1 / den, b = w2 / den;
+  const int per = head_dim / 32;
+  float* p1 = acc + (row * heads + h) * head_dim + lane * per;
+  const __nv_bfloat16* p2 = part + (row * heads + h) * head_dim + lane * per;
+  for (int i = 0; i < per; ++i) p1[i] = p1[i] * a + __bfloat162float(p2[i]) * b;
+  __syncwarp();
+  if (lane == 0) lse_acc[h * ld1 + row] = m + __logf(den);
+}
+
 }  // namespace orl
 
 using namespace orl;
@@ -172,5 +196,18 @@ extern "C" int orl_lse_merge(void* o1, float* lse1, const void* o2, const float*
   lse_merge_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
       static_cast<__nv_bfloat16*>(o1), lse1, static_cast<const __nv_bfloat16*>(o2), lse2, n, ld1, ld2, heads,
       head_dim);
+  return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
+}
+
+extern "C" int orl_lse_merge_acc(float* acc, float* lse_acc, const void* part, const float* lse_part, long long n,
+                                 long long ld1, long long ld2, int heads, int head_dim, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (acc == nullptr || lse_acc == nullptr || part == nullptr || lse_part == nullptr || n < 0 || heads <= 0)
+    return ORL_ERR_ARG;
+  if (head_dim % 32 != 0 || head_dim <= 0) return ORL_ERR_UNSUPPORTED;
+  if (n == 0) return ORL_OK;
+  const long long blocks = (n * heads * 32 + 255) / 256;
+  lse_merge_acc_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      acc, lse_acc, static_cast<const __nv_bfloat16*>(part), lse_part, n, ld1, ld2, heads, head_dim);
   return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
 }

@@ -7,8 +7,9 @@ work per layer is: one gather/pack launch for the K/V of every local segment, on
 (grouped NCCL send/recv on the high-priority NCCL stream) overlapped with the attention of the scenes whose keys are
 all local. The segment list, run tables and work lists are compiled once per (layout, pass, partition) and cached.
 
-Variants the reference also carries but that are not on this path (bounded memory `memory`, `subject_links`, the Ring
-baseline `mode='ring'`, frame-memory selection) raise NotImplementedError here; `shared_pos='adjacent'` likewise.
+The Ring baseline (`mode='ring'`, src/onereel/parallel/ring.py) runs on the same kernels (onereel_b200/ring.py).
+Variants the reference also carries but that are not on this path (bounded memory `memory`, `subject_links`,
+frame-memory selection) raise NotImplementedError here; `shared_pos='adjacent'` likewise.
 """
 from __future__ import annotations
 
@@ -18,7 +19,7 @@ import numpy as np
 import torch
 
 from onereel_b200 import attention as A
-from onereel_b200 import comm, dist as D
+from onereel_b200 import comm, dist as D, ring as R
 from onereel_b200 import scene as S
 from onereel_b200.layout import SceneLayout
 from onereel_b200.rope import qk_norm_rope
@@ -78,8 +79,8 @@ def _layout_key(lay: SceneLayout):
 
 
 def _unsupported(ctx):
-    if ctx.memory or ctx.subject_links or ctx.run_mode == 'ring' or ctx.mode == 'ring':
-        raise NotImplementedError('bounded memory, subject links and the Ring baseline are not on the B200 path')
+    if ctx.memory or ctx.subject_links:
+        raise NotImplementedError('bounded memory and subject links are not on the B200 path')
     if ctx.shared_pos == 'adjacent' or (ctx.shared_pos == 'switch' and ctx.step() >= ctx.shared_switch):
         raise NotImplementedError("shared_pos='adjacent' (shared-key RoPE re-rotation) is not on the B200 path")
 
@@ -130,12 +131,12 @@ class Processor:
         _unsupported(ctx)
         cos, sin = image_rotary_emb
         ctx._rot_full = image_rotary_emb
-        a, b = ctx.own[D.rank()]
+        rows = local_rows(ctx)
         H = attn.heads
         # per-head RMSNorm + rotary embedding of the local rows in one fused kernel (orl_qk_norm_rope)
-        q = qk_norm_rope(attn.to_q(hidden_states).to(torch.bfloat16), attn.norm_q.weight, cos[a:b], sin[a:b], H,
+        q = qk_norm_rope(attn.to_q(hidden_states).to(torch.bfloat16), attn.norm_q.weight, cos[rows], sin[rows], H,
                          attn.norm_q.eps, per_head=True, sin_shift=0)
-        k = qk_norm_rope(attn.to_k(hidden_states).to(torch.bfloat16), attn.norm_k.weight, cos[a:b], sin[a:b], H,
+        k = qk_norm_rope(attn.to_k(hidden_states).to(torch.bfloat16), attn.norm_k.weight, cos[rows], sin[rows], H,
                          attn.norm_k.eps, per_head=True, sin_shift=0)
         v = attn.to_v(hidden_states).unflatten(2, (H, -1))[0].to(torch.bfloat16).contiguous()
         eq, ek, ev = (f(encoder_hidden_states).unflatten(2, (attn.heads, -1))
@@ -147,6 +148,8 @@ class Processor:
         eq, ek, ev = (x[0].to(torch.bfloat16).contiguous() for x in (eq, ek, ev))
         if ctx.run_mode == 'ulysses' or ctx.attn_override is not None:
             hs, ehs = self.ulysses(q, k, v, eq, ek, ev)
+        elif ctx.run_mode == 'ring':
+            hs, ehs = R.attention(ctx.ring, q, k, v, eq, ek, ev, ctx.text_ranges(), id(ctx.layout.extra))
         else:
             hs, ehs = self.scene(q, k, v, eq, ek, ev)
         hs = attn.to_out[1](attn.to_out[0](hs.flatten(1, 2)[None].to(hidden_states.dtype)))
@@ -264,6 +267,12 @@ def plan_parallel(ctx: Context, heads: int):
     if n == 1:
         ctx.run_mode, ctx.own, ctx.path = 'scene', [(0, lay.n_frames * ctx.T)], {}
         return
+    if ctx.mode == 'ring':                       # baseline: USP's Ring with every scene split evenly over the ranks
+        assert not ctx.memory and not ctx.subject_links, 'the ring path runs the halo / frame-memory scene attention'
+        ctx.ring = R.RingPlan(lay, n, ctx.T)
+        ctx.run_mode, ctx.own = 'ring', ctx.ring.own
+        ctx.path = dict(path='ring', V_R=ctx.ring.volume(), V_U=4 * lay.n_frames * ctx.T * (n - 1) / n ** 2)
+        return
     _unsupported(ctx)
     gather = comm.partition(lay, n, ctx.T, 'scene', ctx.counts[True], ctx.memory, ctx.partition)
     ctx.path = comm.choose_path(lay, gather, ctx.T, ctx.theta)
@@ -294,14 +303,15 @@ def _segments(ctx, scenes, qf, kf, vf, eq, ek, ev, text_for):
 
 
 def local_rows(ctx):
-    """hunyuan15.py:457-460: this rank's video rows"""
+    """hunyuan15.py:457-460: this rank's video rows — a token slice, or the ring's permuted rows"""
     a, b = ctx.own[D.rank()]
-    return slice(a, b)
+    return ctx.ring.perm[a:b] if ctx.run_mode == 'ring' else slice(a, b)
 
 
 def gather_rows(ctx, x):
-    """hunyuan15.py:463-466: [B, local rows, C] -> [B, all tokens, C]"""
-    return comm.gather_tokens(x, ctx.own)
+    """hunyuan15.py:463-466: [B, local rows, C] -> [B, all tokens, C] in token order"""
+    x = comm.gather_tokens(x, ctx.own)
+    return x[:, ctx.ring.inv] if ctx.run_mode == 'ring' and D.world() > 1 else x
 
 
 def install_attention(transformer, ctx: Context):

@@ -14,7 +14,7 @@ import torch
 import torch.nn.functional as F
 
 from onereel_b200 import attention as A
-from onereel_b200 import comm, dist as D
+from onereel_b200 import comm, dist as D, ring as R
 from onereel_b200 import scene as S
 from onereel_b200.hunyuan15 import _attend, _layout_key
 from onereel_b200.layout import SceneLayout
@@ -72,17 +72,19 @@ class Processor:
     def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, rotary_emb=None):
         """wan.py:81-108"""
         ctx, T, lay = self.ctx, self.ctx.T, self.ctx.layout
-        if ctx.memory or ctx.run_mode == 'ring':
-            raise NotImplementedError('bounded memory and the Ring baseline are not on the B200 path')
+        if ctx.memory:
+            raise NotImplementedError('bounded memory is not on the B200 path')
         a, b = ctx.own[D.rank()]
         if self.kind == 'cross':
-            pieces = [(j, lo - a, hi - a) for j, (lo, hi) in [(j, (max(lo * T, a), min(hi * T, b)))
-                                                              for j, (lo, hi) in enumerate(lay.ranges)
-                                                              if lo * T < b and hi * T > a]]
+            pieces = ([(j, lo, hi) for j, lo, hi in ctx.ring.local[D.rank()] if hi > lo] if ctx.run_mode == 'ring' else
+                      [(j, lo - a, hi - a) for j, (lo, hi) in [(j, (max(lo * T, a), min(hi * T, b)))
+                                                               for j, (lo, hi) in enumerate(lay.ranges)
+                                                               if lo * T < b and hi * T > a]])
             return torch.cat([self.orig(attn, hidden_states[:, lo:hi],
                                         encoder_hidden_states[:, j * TEXT_LEN:(j + 1) * TEXT_LEN], None, rotary_emb)
                               for j, lo, hi in pieces], 1)
-        cos, sin = (x[:, a:b].reshape(b - a, -1) for x in rotary_emb)
+        rows = ctx.ring.perm[a:b] if ctx.run_mode == 'ring' else slice(a, b)
+        cos, sin = (x[:, rows].reshape(b - a, -1) for x in rotary_emb)
         H = attn.heads
         # hidden-dimension RMSNorm + Wan's interleaved RoPE in one fused kernel (replaces the compiled _qk)
         q = fused_qk_norm_rope(attn.to_q(hidden_states).to(torch.bfloat16), attn.norm_q.weight, cos, sin, H,
@@ -96,6 +98,8 @@ class Processor:
             o = comm.a2a_tokens(self.ranges(qa, ka, va) if r is None else r)
         elif ctx.run_mode == 'ulysses' or D.world() == 1:
             o = comm.a2a_tokens(self.ranges(comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)))
+        elif ctx.run_mode == 'ring':
+            o = R.attention(ctx.ring, q, k, v, tag=id(lay.extra))[0]
         else:
             o = self.scene(q, k, v)
         return attn.to_out[1](attn.to_out[0](o.flatten(1, 2)[None].type_as(hidden_states)))
@@ -157,8 +161,14 @@ def plan_parallel(ctx: Context, heads: int):
     if n == 1:
         ctx.run_mode, ctx.own, ctx.path = 'scene', [(0, lay.n_frames * ctx.T)], {}
         return
-    if ctx.memory or ctx.mode == 'ring':
-        raise NotImplementedError('bounded memory and the Ring baseline are not on the B200 path')
+    if ctx.mode == 'ring':                       # baseline: USP's Ring with every scene split evenly over the ranks
+        assert not ctx.memory, 'the ring path runs the halo / frame-memory scene attention'
+        ctx.ring = R.RingPlan(lay, n, ctx.T)
+        ctx.run_mode, ctx.own = 'ring', ctx.ring.own
+        ctx.path = dict(path='ring', V_R=ctx.ring.volume(), V_U=4 * lay.n_frames * ctx.T * (n - 1) / n ** 2)
+        return
+    if ctx.memory:
+        raise NotImplementedError('bounded memory is not on the B200 path')
     gather = comm.partition(lay, n, ctx.T, 'scene', None, ctx.memory)
     ctx.path = comm.choose_path(lay, gather, ctx.T, ctx.theta)
     ctx.path['ulysses_ok'] = lay.n_frames * ctx.T % n == 0 and heads % n == 0

@@ -9,6 +9,7 @@ tests/dist_onereel_kv_chunks.py, dist_onereel_overlap.py, dist_onereel_gather.py
     one-GPU `ranges` reads the same keys in token order, so it is compared within rel 1e-2;
   - overlap='lse' (local keys during the exchange, LSE merge) within rel 1e-2 of waiting;
   - Ulysses equals the single-GPU result bit for bit; text_sync='all_reduce' equals 'rows' on touched scenes;
+  - the Scene-Ring baseline (mode='ring', Hunyuan with text and Wan) within rel 1e-2 of the single-GPU result;
   - the Eq. 2 chooser ('auto') picks a path and reproduces the single-GPU result.
 Prints PASS lines on rank 0; any failure raises (non-zero exit)."""
 import os
@@ -19,7 +20,7 @@ import torch
 
 sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 
-from onereel_b200 import attention as A, comm, dist as D, hunyuan15 as HY, wan as WN   # noqa: E402
+from onereel_b200 import attention as A, comm, dist as D, hunyuan15 as HY, ring as R, wan as WN   # noqa: E402
 from onereel_b200.layout import SceneLayout                                            # noqa: E402
 
 
@@ -83,6 +84,18 @@ def main():
             wu = WN.Processor(WN.Context(lay, T=T, own=uown), 'self', None, 0)
             wo = comm.a2a_tokens(wu.ranges(*(comm.a2a_heads(x[ua:ub].contiguous()) for x in (q, k, v))))
             assert torch.equal(wo.contiguous(), wref[ua:ub]), (lengths, r, 'wan ulysses')
+        # the Scene-Ring baseline: permuted rows, n - 1 ring steps, LSE merges
+        rctx = HY.Context(lay, mode='ring', T=T, counts={True: counts}, fwd=1)
+        HY.plan_parallel(rctx, H)
+        if n > 1:
+            ra, rb = rctx.own[r]
+            rows = rctx.ring.perm[ra:rb]
+            rv, rt = R.attention(rctx.ring, q[rows].contiguous(), k[rows].contiguous(), v[rows].contiguous(), eq, ek,
+                                 ev, rctx.text_ranges(), id(lay.extra))
+            assert rel(rv, ref_v[rows]) < 1e-2 and rel(rt, ref_t) < 1e-2, (lengths, r, 'ring', rel(rv, ref_v[rows]))
+            wr = R.attention(rctx.ring, q[rows].contiguous(), k[rows].contiguous(), v[rows].contiguous(),
+                             tag=id(lay.extra))[0]
+            assert rel(wr, wref_scene[rows]) < 1e-2, (lengths, r, 'wan ring')
         # the Eq. 2 chooser
         actx = HY.Context(lay, mode='auto', T=T, counts={True: counts}, fwd=1)
         HY.plan_parallel(actx, H)

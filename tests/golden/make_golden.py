@@ -13,6 +13,7 @@ What is recorded (reference file:line in brackets):
                  wan.Processor.ranges/scene (110-152): per packed call, each segment's query and key source rows and
                  the call's cu_seqlens (attention.py:28-29, 65-71). Rows are recorded by running the processor on index
                  tensors (video token t -> t, text row i -> -(i + 1)); the collectives are replaced by row lookups.
+  ring.json      RingPlan chunks / permutation / per-rank rows / key sets (src/onereel/parallel/ring.py:23-60)
   cfg1.npz       BASELINE cfg1 run through hunyuan15.Processor.scene at world 1 in fp32 on the CPU, with the FA varlen
                  call replaced by per-segment fp32 softmax attention: inputs are regenerated from seed 0 by the tests,
                  outputs stored as float32 (every 4th video row, every text row).
@@ -36,6 +37,7 @@ from onereel import attention as A                          # noqa: E402
 from onereel.layout import SceneLayout                        # noqa: E402
 from onereel.models import hunyuan15 as HY, wan as WN         # noqa: E402
 from onereel.parallel import comm, dist as D                  # noqa: E402
+from onereel.parallel import ring as RG                       # noqa: E402
 
 
 def rand_layout(rng, max_scenes=8, max_len=12):
@@ -271,7 +273,24 @@ def gen_cfg1():
     return rec
 
 
+def gen_ring(rng):
+    """RingPlan (src/onereel/parallel/ring.py:23-60) on seeded layouts: chunks, perm, own, local, volume, keys"""
+    out = []
+    for _ in range(40):
+        c = rand_layout(rng, max_scenes=6, max_len=6)
+        lay = make(c)
+        T = rng.choice([3, 7, 16])
+        n = rng.choice([1, 2, 3, 4])
+        plan = RG.RingPlan(lay, n, T, device='cpu')
+        keys = {str(src): {str(j): (None if x is None else x.tolist()) for j, x in plan.keys(src, 'tag').items()}
+                for src in range(n)}
+        out.append(dict(c, T=T, n=n, chunks=plan.chunks, perm=plan.perm.tolist(), inv=plan.inv.tolist(),
+                        own=[list(o) for o in plan.own], local=plan.local, volume=plan.volume(), keys=keys))
+    return out
+
+
 def main():
+    (HERE / 'ring.json').write_text(json.dumps(gen_ring(random.Random(7))))
     rng = random.Random(20261201)
     torch.set_num_threads(os.cpu_count())
     (HERE / 'layout.json').write_text(json.dumps(gen_layout(rng)))

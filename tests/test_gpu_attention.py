@@ -185,3 +185,22 @@ def test_cfg2_full_size_sampled_rows():
     rows = [torch.arange(0, n, 13) for n in lq]
     mx, mean, lmx = compare(out, l, ref_attention(q, k, v, qs, lq, ks, lk, rows=rows), qs)
     assert mx < MAX_ABS and mean < MEAN_ABS and lmx < 1e-3, (mx, mean, lmx)
+
+
+def test_ring_single_rank_matches_scene_path():
+    """the Scene-Ring path on one rank (one step, LSE merge into the fp32 accumulator) against the scene path"""
+    from onereel_b200 import hunyuan15 as HY, ring as R
+    from onereel_b200.layout import SceneLayout
+    lay = SceneLayout([3, 5, 2], halo=1, extra={0: [7], 2: [0]})
+    T, H, Dh, counts = 32, 4, 128, [5, 9, 3]
+    L = lay.n_frames * T
+    q, k, v = rand(L, H, Dh, seed=1), rand(L, H, Dh, seed=2), rand(L, H, Dh, seed=3)
+    eq, ek, ev = rand(17, H, Dh, seed=4), rand(17, H, Dh, seed=5), rand(17, H, Dh, seed=6)
+    ctx = HY.Context(lay, T=T, counts={True: counts}, fwd=1, own=[(0, L)])
+    ref_v, ref_t = HY.Processor(ctx, 0).scene(q, k, v, eq, ek, ev)
+    plan = R.RingPlan(lay, 1, T)
+    rows = plan.perm
+    ov, ot = R.attention(plan, q[rows].contiguous(), k[rows].contiguous(), v[rows].contiguous(), eq, ek, ev,
+                         ctx.text_ranges(), id(lay.extra))
+    rel = lambda x, y: ((x.float() - y.float()).norm() / y.float().norm()).item()
+    assert rel(ov, ref_v[rows]) < 1e-2 and rel(ot, ref_t) < 1e-2

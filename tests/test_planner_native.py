@@ -142,3 +142,17 @@ def test_rank_plans_match_reference_calls():
     finally:
         D.world, D.rank = saved
     assert checked > 100
+
+
+def test_ring_plan_matches_reference():
+    """onereel_b200.ring.RingPlan against the reference's RingPlan (chunks, permutation, rows, volume, key sets)"""
+    from onereel_b200.ring import RingPlan
+    for c in json.loads((G / 'ring.json').read_text()):
+        plan = RingPlan(lay_of(c), c['n'], c['T'], device='cpu')
+        assert [[list(x) for x in ch] for ch in plan.chunks] == c['chunks']
+        assert plan.perm.tolist() == c['perm'] and plan.inv.tolist() == c['inv']
+        assert [list(o) for o in plan.own] == c['own'] and [[list(x) for x in l] for l in plan.local] == c['local']
+        assert plan.volume() == c['volume']
+        for src in range(c['n']):
+            got = {str(j): (None if x is None else x.tolist()) for j, x in plan.keys(src, 'tag').items()}
+            assert got == c['keys'][str(src)]
