@@ -8,8 +8,9 @@ work per layer is: one gather/pack launch for the K/V of every local segment, on
 all local. The segment list, run tables and work lists are compiled once per (layout, pass, partition) and cached.
 
 The Ring baseline (`mode='ring'`, src/onereel/parallel/ring.py) runs on the same kernels (onereel_b200/ring.py).
-Variants the reference also carries but that are not on this path (bounded memory `memory`, `subject_links`,
-frame-memory selection) raise NotImplementedError here; `shared_pos='adjacent'` likewise.
+Frame memory (`frame_memory`, onereel_b200/frame_memory.py) plugs in through install_attention's hooks. Variants the
+reference also carries but that are not on this path (bounded memory `memory`, `subject_links`) raise
+NotImplementedError here; `shared_pos='adjacent'` likewise.
 """
 from __future__ import annotations
 
@@ -315,15 +316,47 @@ def gather_rows(ctx, x):
 
 
 def install_attention(transformer, ctx: Context):
-    """the attention part of hunyuan15.install (407-440): a Processor on every block, the forward counter, and the
-    token shard / gather hooks of the first / last block when parallel. `transformer` is the diffusers
-    HunyuanVideo15Transformer3DModel (or any module with .transformer_blocks[i].attn.set_processor)."""
+    """the attention part of hunyuan15.install (407-440, _observe 469-495): a Processor on every block; the forward
+    counter and the frame-memory step / layer / pooling hooks; the token shard / gather hooks of the first / last block
+    when parallel. `transformer` is the diffusers HunyuanVideo15Transformer3DModel (or any module with
+    .transformer_blocks[i].attn.set_processor); blocks return (hidden states, text states)."""
     for i, blk in enumerate(transformer.transformer_blocks):
         blk.attn.set_processor(Processor(ctx, i))
 
     def pre(m, args, kw):
         ctx.fwd += 1
+        if ctx.frame_memory is not None:
+            ctx.frame_memory.begin_step(ctx.step())
+
+    def post(m, args, kw, out):
+        if ctx.frame_memory is not None and ctx.cond():
+            ctx.frame_memory.finish()
     transformer.register_forward_pre_hook(pre, with_kwargs=True)
+    transformer.register_forward_hook(post, with_kwargs=True)
+    frame_of_row = {}
+
+    def hooks(i):
+        def block_pre(m, args):
+            if ctx.frame_memory is not None:
+                ctx.frame_memory.use_layer(i)
+
+        def block_post(m, args, out):
+            fm = ctx.frame_memory
+            if fm is None or not fm.observes(i) or not ctx.cond():
+                return
+            hs = out[0][0]
+            key = (tuple(ctx.own[D.rank()]), ctx.run_mode)
+            if key not in frame_of_row:
+                frame_of_row.clear()
+                a, b = ctx.own[D.rank()]
+                rows = ctx.ring.perm[a:b] if ctx.run_mode == 'ring' else torch.arange(a, b, device=hs.device)
+                frame_of_row[key] = rows.to(hs.device) // ctx.T
+            fm.collect(frame_of_row[key], hs, i)
+        return block_pre, block_post
+    for i, blk in enumerate(transformer.transformer_blocks):
+        bp, bq = hooks(i)
+        blk.register_forward_pre_hook(bp)
+        blk.register_forward_hook(bq)
     if D.world() > 1:
         def shard(m, args):
             return (args[0][:, local_rows(ctx)],) + tuple(args[1:])

@@ -13,6 +13,7 @@ What is recorded (reference file:line in brackets):
                  wan.Processor.ranges/scene (110-152): per packed call, each segment's query and key source rows and
                  the call's cu_seqlens (attention.py:28-29, 65-71). Rows are recorded by running the processor on index
                  tensors (video token t -> t, text row i -> -(i + 1)); the collectives are replaced by row lookups.
+  frame_memory.json  FrameMemory selections and extra frames (src/onereel/frame_memory.py:24-132) on seeded features
   ring.json      RingPlan chunks / permutation / per-rank rows / key sets (src/onereel/parallel/ring.py:23-60)
   cfg1.npz       BASELINE cfg1 run through hunyuan15.Processor.scene at world 1 in fp32 on the CPU, with the FA varlen
                  call replaced by per-segment fp32 softmax attention: inputs are regenerated from seed 0 by the tests,
@@ -38,6 +39,7 @@ from onereel.layout import SceneLayout                        # noqa: E402
 from onereel.models import hunyuan15 as HY, wan as WN         # noqa: E402
 from onereel.parallel import comm, dist as D                  # noqa: E402
 from onereel.parallel import ring as RG                       # noqa: E402
+from onereel.frame_memory import FrameMemory                  # noqa: E402
 
 
 def rand_layout(rng, max_scenes=8, max_len=12):
@@ -289,8 +291,40 @@ def gen_ring(rng):
     return out
 
 
+def gen_frame_memory(rng):
+    """FrameMemory (src/onereel/frame_memory.py:24-132): selections on seeded per-frame features (CPU fp32), and the
+    extra frames a full reset / collect / finish / begin_step cycle produces"""
+    out = []
+    for i in range(30):
+        c = rand_layout(rng, max_scenes=6, max_len=10)
+        lay = make(c)
+        budget = rng.randint(2, 6)
+        cands = rng.choice(['all', 'boundary'])
+        sink = tuple(sorted(rng.sample(range(lay.n_frames), min(rng.randint(0, 1), lay.n_frames))))
+        if len(sink) >= budget:
+            sink = ()
+        C = rng.choice([8, 32])
+        g = torch.Generator().manual_seed(100 + i)
+        rows_per_frame = rng.randint(1, 4)
+        frame = torch.arange(lay.n_frames).repeat_interleave(rows_per_frame)
+        hs = torch.randn(len(frame), C, generator=g)
+        fm = FrameMemory(budget=budget, candidates=cands, sink=sink, fallback=(1, 'adj'))
+        lay.extra = {}
+        fm.reset(lay, n_layers=4)
+        first = dict(lay.extra)
+        fm.begin_step(0)
+        fm.collect(frame, hs)
+        fm.finish()
+        fm.begin_step(1)
+        out.append(dict(lengths=c['lengths'], budget=budget, candidates=cands, sink=list(sink), C=C, seed=100 + i,
+                        rows_per_frame=rows_per_frame, first={str(k): v for k, v in first.items()},
+                        reps=fm.history[-1], extra={str(k): v for k, v in lay.extra.items()}))
+    return out
+
+
 def main():
     (HERE / 'ring.json').write_text(json.dumps(gen_ring(random.Random(7))))
+    (HERE / 'frame_memory.json').write_text(json.dumps(gen_frame_memory(random.Random(11))))
     rng = random.Random(20261201)
     torch.set_num_threads(os.cpu_count())
     (HERE / 'layout.json').write_text(json.dumps(gen_layout(rng)))
