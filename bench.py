@@ -33,6 +33,9 @@ SMALL = dict(lengths=[8, 6], T=1590, text=128, heads=16, dim=128, memory=[0, 8])
 # BASELINE cfg3: Wan2.2-TI2V-5B-shaped layer through the joint [video | text] scene path, sharded (strong scaling)
 CFG3 = dict(lengths=[3, 12, 5, 9, 4, 8], T=880, text=256, heads=24, dim=128, memory=[0, 3, 15, 20])
 # BASELINE cfg4: full denoising step of the HunyuanVideo-1.5-architecture stand-in (4 scenes x 31 frames, 480p)
+# BASELINE cfg5: Wan2.2-shaped long-video stress layer, S scenes x 31 latent frames at 880 tokens per frame, 24 x 128
+# heads, frame memory 4 (the first frame of the first four scenes), no joint text (Wan self-attention)
+CFG5 = dict(scene_frames=31, T=880, text=0, heads=24, dim=128)
 CFG4 = dict(lengths=[31, 31, 31, 31], T=1590, text=128, heads=16, dim=128, memory=[0, 31, 62, 93], hidden=2048,
             blocks=54, frame_hw=(30, 53))
 METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
@@ -133,20 +136,20 @@ def run_reference(args):
 
 
 def make_inputs(lay, T, counts, H, Dh, dev, rows=None, seed=0):
-    """Q/K RMS-normed over D from N(0, 1) (unit weight), V ~ N(0, 1), seeded on the CPU (BASELINE cfg2); rows = the
-    rank's video token range (a, b), drawn from a generator seeded by (seed, a) so ranks draw only their own rows"""
-    g = torch.Generator().manual_seed(seed * 1000003 + (rows[0] if rows else 0))
+    """Q/K RMS-normed over D from N(0, 1) (unit weight), V ~ N(0, 1) (BASELINE cfg2), drawn on the device from a
+    generator seeded by (seed, first row) so every rank draws only its own rows = the rank's video range (a, b)"""
+    g = torch.Generator(device=dev).manual_seed(seed * 1000003 + (rows[0] if rows else 0))
     L, Nt = lay.n_frames * T, sum(counts)
     a, b = rows or (0, L)
 
     def qk(n):
-        x = torch.randn(n, H, Dh, generator=g)
+        x = torch.randn(n, H, Dh, generator=g, device=dev)
         return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
     q, k = qk(b - a), qk(b - a)
-    v = torch.randn(b - a, H, Dh, generator=g).to(torch.bfloat16)
+    v = torch.randn(b - a, H, Dh, generator=g, device=dev).to(torch.bfloat16)
     eq, ek = qk(Nt), qk(Nt)
-    ev = torch.randn(Nt, H, Dh, generator=g).to(torch.bfloat16)
-    return [x.contiguous().to(dev) for x in (q, k, v, eq, ek, ev)]
+    ev = torch.randn(Nt, H, Dh, generator=g, device=dev).to(torch.bfloat16)
+    return [x.contiguous() for x in (q, k, v, eq, ek, ev)]
 
 
 def main():
@@ -159,19 +162,23 @@ def main():
                     help='parallel path for N > 1: auto (the Eq. 2 chooser), scene or ulysses; a comma list runs '
                          'each in turn and prints one line per mode')
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small', 'cfg3', 'cfg4'],
+    ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg (auto for cfg5)')
+    ap.add_argument('--scenes', default='16', help='cfg5: scene counts to sweep (comma list)')
+    ap.add_argument('--workload', default='cfg2', choices=['cfg2', 'small', 'cfg3', 'cfg4', 'cfg5'],
                     help='cfg2 (default bench line; weak scaling over N); small: the first two scenes of cfg2, for '
                          'profiler captures; cfg3: BASELINE cfg3 layer sharded over N (strong scaling); cfg4: one '
-                         'full DiT denoising step of the stand-in (strong scaling)')
+                         'full DiT denoising step of the stand-in (strong scaling); cfg5: Wan-shaped stress layer '
+                         'with --scenes S (strong scaling)')
     args = ap.parse_args()
     if args.impl == 'reference':
         return run_reference(args)
     if args.workload == 'cfg4':
         return run_dit_step(args)
-    modes = args.mode.split(',')
-    for i, mode in enumerate(modes):
-        args.mode = mode
-        run_layer(args, last=i == len(modes) - 1)
+    runs = [(m, sc) for sc in (args.scenes.split(',') if args.workload == 'cfg5' else [None])
+            for m in args.mode.split(',')]
+    for i, (mode, sc) in enumerate(runs):
+        args.mode, args.n_scenes = mode, (int(sc) if sc else None)
+        run_layer(args, last=i == len(runs) - 1)
 
 
 def run_layer(args, last=True):
@@ -191,19 +198,42 @@ def run_layer(args, last=True):
         build()                      # other ranks load the library rank 0 built
     dev = torch.device('cuda', local)
 
-    cfg = dict({'cfg2': CFG2, 'small': SMALL, 'cfg3': CFG3}[args.workload])
-    if args.workload != 'cfg3':
+    if args.workload == 'cfg5':
+        S_ = args.n_scenes
+        cfg = dict(CFG5, lengths=[CFG5['scene_frames']] * S_,
+                   memory=[j * CFG5['scene_frames'] for j in range(min(4, S_))])
+    else:
+        cfg = dict({'cfg2': CFG2, 'small': SMALL, 'cfg3': CFG3}[args.workload])
+    if args.workload not in ('cfg3', 'cfg5'):
         # weak scaling: N GPUs run cfg2's scene set repeated N times (per-GPU work fixed); every scene reads the frame
         # memory of the first copy, so ranks exchange those rows (the path's real K/V gathering step)
         cfg['lengths'] = cfg['lengths'] * world
     lay = cfg_layout(cfg)
     T, H, Dh = cfg['T'], cfg['heads'], cfg['dim']
     counts = [cfg['text']] * lay.n_scenes
-    ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts}, fwd=1)
-    HY.plan_parallel(ctx, H)
+    wan = args.workload == 'cfg5'
+    if wan:
+        from onereel_b200 import comm, wan as WN
+        ctx = WN.Context(lay, mode=args.mode, T=T)
+        WN.plan_parallel(ctx, H)
+        wproc = WN.Processor(ctx, 'self', None, 0)
+
+        class _WanCall:
+            """Wan self-attention of the local rows (wan.py:97-107 dispatch) in the processor-call shape"""
+            def scene(self, q, k, v, *text):
+                if ctx.run_mode == 'ulysses' or world == 1:
+                    o = comm.a2a_tokens(wproc.ranges(comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)))
+                else:
+                    o = wproc.scene(q, k, v)
+                return o, text[0]
+            ulysses = scene
+        proc = _WanCall()
+    else:
+        ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts}, fwd=1)
+        HY.plan_parallel(ctx, H)
+        proc = HY.Processor(ctx, 0)
     own = ctx.own[rank]
     q, k, v, eq, ek, ev = make_inputs(lay, T, counts, H, Dh, dev, own, seed=0)
-    proc = HY.Processor(ctx, 0)
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -240,40 +270,62 @@ def run_layer(args, last=True):
     ms = t0.elapsed_time(t1) / args.steps
     attn_ms = sum(a.elapsed_time(b) for a, b, _ in timing) / args.steps
 
-    # end to end through the public API with host buffers: H2D of the layer's local q/k/v and the text q/k/v from
-    # pinned memory, the processor call, D2H of its outputs, every step inside the timed region
-    host_in = [x.cpu().pin_memory() for x in (q, k, v, eq, ek, ev)]
-    dev_in = [torch.empty_like(x) for x in (q, k, v, eq, ek, ev)]
-    host_out = [torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
-                torch.empty(eq.shape, dtype=eq.dtype, pin_memory=True)]
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not (args.no_e2e or args.workload == 'cfg5'):
+        # end to end through the public API with host buffers: every step copies its layer's local q/k/v and the text
+        # q/k/v host->device from pinned memory, calls the processor, and copies its outputs device->host. Steps are
+        # pipelined the way a caller streaming layers would run them: two device input buffers, H2D on one copy stream,
+        # D2H on another, so step i+1's inputs travel while step i computes and step i-1's outputs return.
+        host_in = [x.cpu().pin_memory() for x in (q, k, v, eq, ek, ev)]
+        dev_in = [[torch.empty_like(x) for x in (q, k, v, eq, ek, ev)] for _ in range(2)]
+        host_out = [[torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
+                     torch.empty(eq.shape, dtype=eq.dtype, pin_memory=True)] for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        done[0].record(stream)
+        done[1].record(stream)
 
-    def e2e_step():
-        for d_, h_ in zip(dev_in, host_in):
-            d_.copy_(h_, non_blocking=True)
-        ov, ot = (proc.ulysses if ctx.run_mode == 'ulysses' else proc.scene)(*dev_in)
-        host_out[0].copy_(ov, non_blocking=True)
-        host_out[1].copy_(ot, non_blocking=True)
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    e_steps = max(3, args.steps // 4)
-    D.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    D.barrier()
-    A.check()
-    e2e_ms = e0.elapsed_time(e1) / e_steps
+        def e2e_step(i):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(done[b])                      # step i - 2 has finished reading this buffer
+                for d_, h_ in zip(dev_in[b], host_in):
+                    d_.copy_(h_, non_blocking=True)
+                ready[b].record(s_in)
+            stream.wait_event(ready[b])
+            ov, ot = (proc.ulysses if ctx.run_mode == 'ulysses' else proc.scene)(*dev_in[b])
+            done[b].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done[b])
+                ov.record_stream(s_out)
+                ot.record_stream(s_out)
+                host_out[b][0].copy_(ov, non_blocking=True)
+                host_out[b][1].copy_(ot, non_blocking=True)
+        for i in range(2):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        e_steps = max(4, args.steps // 4)
+        D.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s_in)
+        for i in range(e_steps):
+            e2e_step(i)
+        e1.record(s_out)
+        torch.cuda.synchronize()
+        D.barrier()
+        A.check()
+        e2e_ms = e0.elapsed_time(e1) / e_steps
+        h2d = sum(x.numel() * x.element_size() for x in host_in)
+        d2h = sum(x.numel() * x.element_size() for x in host_out[0])
 
     total_flops = rank_flops
     if world > 1:
         import torch.distributed as dist
-        t = torch.tensor([ms, attn_ms, e2e_ms], device=dev)
+        t = torch.tensor([ms, attn_ms, e2e_ms or 0.0], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, attn_ms_max, e2e_ms = t.tolist()
+        e2e_ms = e2e_ms or None
         f = torch.tensor([rank_flops], dtype=torch.float64, device=dev)
         dist.all_reduce(f)
         total_flops = f.item()
@@ -286,22 +338,25 @@ def run_layer(args, last=True):
     cb = None
     if not args.no_cpu_baseline and args.workload == 'cfg2' and world == 1:
         cb, _ = cpu_baseline()
-    h2d = sum(x.numel() * x.element_size() for x in host_in)
-    d2h = sum(x.numel() * x.element_size() for x in host_out)
     line = dict(metric=METRIC, value=total_flops / (ms * 1e-3) / 1e12, unit='TFLOP/s', n_gpus=world,
                 steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True,
-                scaling='strong' if args.workload == 'cfg3' else 'weak',
+                scaling='strong' if args.workload in ('cfg3', 'cfg5') else 'weak',
                 vs_baseline=None, dtype='bf16', data='synthetic (seeded; Q/K RMS-normed N(0,1), V N(0,1))',
-                config=dict(workload=(f'{args.workload}: one HunyuanVideo-1.5-shaped scene-attention layer through '
-                                      'hunyuan15.Processor.scene (pack K/V + attention' +
+                config=dict(workload=(f'{args.workload}: one ' + ('Wan2.2-shaped self-attention layer through '
+                                      'wan.Processor' if wan else 'HunyuanVideo-1.5-shaped scene-attention layer through '
+                                      'hunyuan15.Processor.scene') + ' (pack K/V + attention' +
                                       (', K/V exchange over NCCL' if world > 1 else '') + ')'),
                             layout=dict(cfg, scenes=lay.n_scenes), run_mode=ctx.run_mode, path=ctx.path,
                             own=ctx.own, useful_tflop_per_step=total_flops / 1e12,
-                            parallelism=(f'{ctx.run_mode} x{world} ' + ('(strong: cfg3 fixed)' if args.workload == 'cfg3'
+                            parallelism=(f'{ctx.run_mode} x{world} ' + ('(strong: layout fixed)'
+                                         if args.workload in ('cfg3', 'cfg5')
                                          else '(weak: cfg2 scene set repeated per GPU)') if world > 1 else 'single'),
                             l2='inputs larger than L2 (q/k/v 203 MB each per GPU, packed K/V ~486 MB each)'),
-                e2e=dict(value=total_flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s', ms_per_step=e2e_ms,
-                         h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
+                e2e=None if e2e_ms is None else dict(value=total_flops / (e2e_ms * 1e-3) / 1e12, unit='TFLOP/s',
+                         ms_per_step=e2e_ms,
+                         h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                         note='processor call with pinned H2D inputs / D2H outputs every step; consecutive steps '
+                              'pipelined on separate copy streams (double-buffered inputs)'),
                 roofline=dict(bound='tensor', achieved=achieved, peak=peak_burst, unit='TFLOP/s',
                               frac=achieved / peak_burst, traffic=None,
                               frac_of_sustained=achieved / peak_sus if peak_sus else None,
