@@ -458,10 +458,17 @@ static int launch_attn(const void* q, const void* k, const void* v, void* out, f
   if ((rc = make_rows_map(&mv, v, nk, heads * D)) != ORL_OK) return rc;
   static std::once_flag once;
   static cudaError_t attr_rc = cudaSuccess;
+  static int launch_regs = 0;
   std::call_once(once, [] {
     attr_rc = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaFuncAttributes fa{};
+    if (attr_rc == cudaSuccess) attr_rc = cudaFuncGetAttributes(&fa, attn_fwd_kernel<D>);
+    launch_regs = fa.numRegs;
   });
   if (attr_rc != cudaSuccess) return ORL_ERR_LAUNCH;
+  // the setmaxnreg split assumes exactly kLaunchRegs registers per thread at launch; any other count could leave
+  // the increasing warpgroups waiting for registers that were never freed, so such a build is never launched
+  if (launch_regs != kLaunchRegs) return ORL_ERR_UNSUPPORTED;
   const float scale_log2 = scale * 1.4426950408889634f;
   attn_fwd_kernel<D><<<n_items, kThreads, C::kSmemBytes, stream>>>(
       mq, mk, mv, work, static_cast<__nv_bfloat16*>(out), lse, nq, heads, scale_log2, err);
