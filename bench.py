@@ -161,6 +161,9 @@ def main():
     ap.add_argument('--mode', default='auto',
                     help='parallel path for N > 1: auto (the Eq. 2 chooser), scene or ulysses; a comma list runs '
                          'each in turn and prints one line per mode')
+    ap.add_argument('--overlap', default='none', choices=['none', 'lse'],
+                    help="K/V gathering: 'lse' attends far scenes to their local keys while the exchange is in flight "
+                         "and merges by log-sum-exp (Context.overlap of the reference)")
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg (auto for cfg5)')
     ap.add_argument('--scenes', default='16', help='cfg5: scene counts to sweep (comma list)')
@@ -229,7 +232,7 @@ def run_layer(args, last=True):
             ulysses = scene
         proc = _WanCall()
     else:
-        ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts}, fwd=1)
+        ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts}, fwd=1, overlap=args.overlap)
         HY.plan_parallel(ctx, H)
         proc = HY.Processor(ctx, 0)
     own = ctx.own[rank]
@@ -347,6 +350,7 @@ def run_layer(args, last=True):
                                       'hunyuan15.Processor.scene') + ' (pack K/V + attention' +
                                       (', K/V exchange over NCCL' if world > 1 else '') + ')'),
                             layout=dict(cfg, scenes=lay.n_scenes), run_mode=ctx.run_mode, path=ctx.path,
+                            overlap=args.overlap,
                             own=ctx.own, useful_tflop_per_step=total_flops / 1e12,
                             parallelism=(f'{ctx.run_mode} x{world} ' + ('(strong: layout fixed)'
                                          if args.workload in ('cfg3', 'cfg5')
