@@ -39,6 +39,8 @@ CFG5 = dict(scene_frames=31, T=880, text=0, heads=24, dim=128)
 CFG4 = dict(lengths=[31, 31, 31, 31], T=1590, text=128, heads=16, dim=128, memory=[0, 31, 62, 93], hidden=2048,
             blocks=54, frame_hw=(30, 53))
 METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
+# DRAM bytes / algorithmic bytes of the attention kernel, from the small-case ncu capture (profiles/attn_fwd_cfg2.md)
+TRAFFIC_PER_ALG_BYTE = 376.64 / 392.9
 
 
 def cfg_layout(cfg):
@@ -254,6 +256,14 @@ def run_layer(args, last=True):
     torch.cuda.synchronize()
     rank_flops = sum(f for _, _, f in S.TIMING)
     S.TIMING = None
+    # algorithmic bytes of the attention launches: every query row read and its output written once, every segment's
+    # keys and values read once per head (H * D * 2 bytes per row)
+    attn_bytes = 0
+    if ctx.run_mode == 'scene' and not wan:
+        p_ = proc._plan(H, Dh, dev, ctx.overlap == 'lse')
+        for pl in (p_.near, p_.far, p_.far_local, p_.far_remote):
+            if pl is not None:
+                attn_bytes += sum(2 * a + 2 * b for a, b in zip(pl.lq, pl.lk)) * H * Dh * 2
 
     with Clocks(local) as clk:
         D.barrier()
@@ -362,7 +372,12 @@ def run_layer(args, last=True):
                          note='processor call with pinned H2D inputs / D2H outputs every step; consecutive steps '
                               'pipelined on separate copy streams (double-buffered inputs)'),
                 roofline=dict(bound='tensor', achieved=achieved, peak=peak_burst, unit='TFLOP/s',
-                              frac=achieved / peak_burst, traffic=None,
+                              frac=achieved / peak_burst,
+                              traffic=(attn_bytes * TRAFFIC_PER_ALG_BYTE if args.workload == 'cfg2' and world == 1
+                                       else None),
+                              traffic_note='bytes per step of the attention launches: their algorithmic bytes (Q + O '
+                                           '+ K/V once per segment) x the DRAM/algorithmic ratio of the small-case '
+                                           'ncu capture (profiles/attn_fwd_cfg2.md)',
                               frac_of_sustained=achieved / peak_sus if peak_sus else None,
                               kernel='attn_fwd_kernel<128> (all attention launches of a step, rank 0)',
                               peak_source=f'{peak_kind} bf16 burst'),
