@@ -59,6 +59,11 @@ ORL_API const char* orl_error_string(int code);
 /* Bits the kernels set in the caller's error word when a bounded wait gave up (the kernel then winds down). */
 ORL_API int orl_error_bits_describe(int bits, char* buf, int cap);
 
+/* Failure-path self test of the kernels' bounded waits: a one-CTA kernel waits on an mbarrier nothing arrives at,
+ * gives up after limit_ns (<= 1 s) and writes the timeout bits to status_dev (nonzero = the wait ran out, as it
+ * must). Has no counterpart in the reference (which has no device-side failure detection). */
+ORL_API int orl_selftest_timeout(int* status_dev, unsigned long long limit_ns, void* stream);
+
 /* Work list of a packed varlen call: replaces the scheduling FlashAttention does internally for
  * attention.py:39-43. cu_q / cu_k: HOST int32 [n_seg + 1] (attention.py:28-29 cu_seqlens). Writes up to
  * `capacity` items (largest key range first; items of one segment and head adjacent) and returns their count.

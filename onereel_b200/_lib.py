@@ -51,6 +51,7 @@ SIGNATURES = {
     'orl_version': (ctypes.c_char_p, []),
     'orl_error_string': (ctypes.c_char_p, [c_int]),
     'orl_error_bits_describe': (c_int, [c_int, ctypes.c_char_p, c_int]),
+    'orl_selftest_timeout': (c_int, [c_vp, ctypes.c_ulonglong, c_vp]),
     'orl_attn_plan': (c_int, [P_I32, P_I32, c_int, c_int, c_vp, c_int]),
     'orl_attn_plan_ranges': (c_int, [P_I32, P_I32, P_I32, P_I32, c_int, c_int, c_vp, c_int]),
     'orl_attn_fwd': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_int, c_int, c_float, c_vp, c_int, c_vp,

@@ -35,3 +35,31 @@ extern "C" int orl_error_bits_describe(int bits, char* buf, int cap) {
     if (bits & e.bit) n += snprintf(buf + n, n < cap ? cap - n : 0, "%s%s", n ? "; " : "", e.what);
   return ORL_OK;
 }
+
+// Failure-path self test: one CTA initialises an mbarrier that nothing arrives at and waits on it with the kernel's
+// bounded wait shortened to limit_ns; the wait gives up, the kernel records the timeout bit and returns. The host
+// reads the status: a pipeline wait that runs out ends the kernel with an error word, never a hang or a trap.
+namespace {
+__global__ void selftest_timeout_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) unsigned long long bar;
+  if (threadIdx.x != 0) return;
+  const uint32_t b = orl::smem_u32(&bar);
+  orl::mbar_init(b, 1);
+  orl::fence_mbar_init();
+  const unsigned long long t0 = orl::global_ns();
+  int bits = 0;
+  while (!orl::mbar_try_wait(b, 0)) {
+    if (orl::global_ns() - t0 > limit_ns) {
+      bits |= orl::kErrTimeoutSoftmax;
+      break;
+    }
+  }
+  *status = bits;
+}
+}  // namespace
+
+extern "C" int orl_selftest_timeout(int* status_dev, unsigned long long limit_ns, void* stream) {
+  if (status_dev == nullptr || limit_ns == 0 || limit_ns > orl::kWaitLimitNs) return ORL_ERR_ARG;
+  selftest_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status_dev, limit_ns);
+  return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
+}

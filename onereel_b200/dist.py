@@ -79,3 +79,18 @@ def shutdown():
     if _ON and dist.is_initialized():
         dist.destroy_process_group()
     _ON, _GROUP = False, None
+
+
+def check_consistent(what: str, obj) -> None:
+    """every rank must hold the same `obj` (a plan: layout, partition, chosen path); ranks that disagree would post
+    mismatched exchanges and wait on each other. Compares a digest of obj across ranks (all_gather_object) and raises
+    on every rank if any differs."""
+    if not _ON or world() == 1:
+        return
+    import hashlib
+    import pickle
+    digest = hashlib.sha256(pickle.dumps(obj)).hexdigest()
+    digests = all_gather_object(digest)
+    if len(set(digests)) > 1:
+        bad = [r for r, d in enumerate(digests) if d != digests[0]]
+        raise RuntimeError(f'{what} differs across ranks (ranks {bad} disagree with rank 0)')

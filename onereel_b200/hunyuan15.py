@@ -281,6 +281,9 @@ def plan_parallel(ctx: Context, heads: int):
     ctx.run_mode = ctx.mode if ctx.mode != 'auto' else ctx.path['path'] if ctx.path['ulysses_ok'] else 'scene'
     assert ctx.run_mode != 'ulysses' or ctx.path['ulysses_ok'], f'Ulysses needs video tokens and heads divisible by {n}'
     ctx.own = gather if ctx.run_mode == 'scene' else comm.partition(lay, n, ctx.T, 'ulysses')
+    # a rank planning from a different layout or text would post mismatched exchanges: fail on every rank instead
+    D.check_consistent('hunyuan15 parallel plan', (_layout_key(lay), ctx.T, ctx.run_mode, [tuple(o) for o in ctx.own],
+                                                   [tuple(ctx.counts.get(c, ())) for c in (True, False)]))
 
 
 _plan_parallel = plan_parallel      # the reference's private name (hunyuan15.py:553)

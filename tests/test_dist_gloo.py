@@ -90,3 +90,74 @@ def test_collectives_on_gloo(world):
         p.join(timeout=60)
     errors = [f'rank {r}:\n{e}' for r, e in results if e]
     assert not errors, '\n'.join(errors)
+
+
+def _mismatch_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                          LOCAL_RANK=str(rank))
+        from onereel_b200 import dist as D, hunyuan15 as HY
+        from onereel_b200.layout import SceneLayout
+        D.init('gloo', timeout_s=30)
+        lengths = [3, 5, 2] if rank == 0 else [3, 5, 3]          # rank 1 planned from another request
+        ctx = HY.Context(SceneLayout(lengths, halo=1), mode='scene', T=16, counts={True: [4, 4, 4]})
+        try:
+            HY.plan_parallel(ctx, 4)
+            q.put((rank, 'no error raised'))
+        except RuntimeError as e:
+            q.put((rank, None if 'differs across ranks' in str(e) else repr(e)))
+        D.shutdown()
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def test_mismatched_plans_fail_on_every_rank():
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mismatch_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(e is None for _, e in results), results
+
+
+def _early_exit_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                          LOCAL_RANK=str(rank))
+        import time
+        from onereel_b200 import comm, dist as D
+        D.init('gloo', timeout_s=10)
+        D.barrier()
+        if rank == 1:
+            q.put((rank, None))
+            q.close()
+            q.join_thread()                                        # the result is delivered before the rank leaves
+            os._exit(0)                                            # leaves between steps, nothing in flight
+        t0 = time.time()
+        try:
+            comm.gather_tokens(torch.zeros(1, 4, 2), [(0, 4), (4, 8)])
+            q.put((rank, 'collective with a departed rank returned'))
+        except Exception:
+            q.put((rank, None if time.time() - t0 < 120 else 'detected too late'))
+        q.close()
+        q.join_thread()
+        os._exit(0)
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def test_departed_rank_is_detected_not_waited_for():
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_early_exit_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(e is None for _, e in results), results
