@@ -142,6 +142,13 @@ ORL_API int orl_qk_norm_rope(const void* x, void* y, const void* weight, const f
                              long long rows, int heads, int head_dim, int per_head, float eps, int sin_shift,
                              long long rope_ld, const int32_t* row_map, void* stream);
 
+/* In-place rotary rotation of listed rows (no norm), for moving shared-frame keys of a packed K to their adjacent
+ * temporal positions (hunyuan15.py:127-150 `_move_shared`, which applies R(-src) then R(dst) with two
+ * apply_rotary_emb calls): x [*, heads * head_dim] bf16; row rows[i] rotated by table row i of cos_t / sin_t
+ * (fp32 [n_rows, rope_ld], pair i by cos[2i], sin[2i + sin_shift]). */
+ORL_API int orl_rope_rows(void* x, const int32_t* rows, long long n_rows, int heads, int head_dim, const float* cos_t,
+                          const float* sin_t, long long rope_ld, int sin_shift, void* stream);
+
 /* ---------------------------------------------------------------- native planner (comm.py:18-112, layout.py:54-78) */
 
 /* A scene layout (layout.py:10-18 SceneLayout): lengths[n_scenes] latent frames per scene, halo frames of the

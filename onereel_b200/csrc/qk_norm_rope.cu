@@ -81,6 +81,32 @@ __global__ void qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bf
   }
 }
 
+// In-place rotation of listed rows (no norm): row rows[i] of x is rotated with table row i (pairs as above). Used to
+// move shared-frame keys of a packed K to their adjacent temporal positions (hunyuan15.py:127-150 `_move_shared`:
+// the two rotations R(-src) then R(dst) composed into one table by the host).
+__global__ void rope_rows_kernel(__nv_bfloat16* __restrict__ x, const int32_t* __restrict__ rows, long long n_rows,
+                                 int hidden, int head_dim, const float* __restrict__ cos_t,
+                                 const float* __restrict__ sin_t, long long rope_ld, int sin_shift) {
+  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_id >= n_rows) return;
+  __nv_bfloat16* xr = x + static_cast<long long>(rows[warp_id]) * hidden;
+  const float* cr = cos_t + warp_id * rope_ld;
+  const float* sr = sin_t + warp_id * rope_ld;
+  for (int e = lane * 8; e < hidden; e += 32 * 8) {
+    uint4 raw = *reinterpret_cast<const uint4*>(xr + e);
+    __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h2[i]);
+      const int d = (e + 2 * i) % head_dim;
+      const float cs = cr[d], sn = sr[d + sin_shift];
+      h2[i] = __floats2bfloat162_rn(f.x * cs - f.y * sn, f.x * sn + f.y * cs);
+    }
+    *reinterpret_cast<uint4*>(xr + e) = raw;
+  }
+}
+
 }  // namespace orl
 
 using namespace orl;
@@ -113,5 +139,22 @@ extern "C" int orl_qk_norm_rope(const void* x, void* y, const void* weight, cons
   else if (chunks <= 16) ORL_QKNR(16);
   else return ORL_ERR_UNSUPPORTED;
 #undef ORL_QKNR
+  return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
+}
+
+extern "C" int orl_rope_rows(void* x, const int32_t* rows, long long n_rows, int heads, int head_dim,
+                             const float* cos_t, const float* sin_t, long long rope_ld, int sin_shift,
+                             void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (x == nullptr || cos_t == nullptr || sin_t == nullptr || (n_rows > 0 && rows == nullptr)) return ORL_ERR_ARG;
+  if (n_rows < 0 || heads <= 0 || head_dim <= 0 || (head_dim & 7) || sin_shift < 0 || sin_shift > 1 ||
+      rope_ld < head_dim)
+    return ORL_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return ORL_ERR_ALIGN;
+  if (n_rows == 0) return ORL_OK;
+  const long long blocks = (n_rows * 32 + 255) / 256;
+  rope_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<__nv_bfloat16*>(x), rows, n_rows,
+                                                                      heads * head_dim, head_dim, cos_t, sin_t,
+                                                                      rope_ld, sin_shift);
   return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
 }

@@ -8,9 +8,10 @@ work per layer is: one gather/pack launch for the K/V of every local segment, on
 all local. The segment list, run tables and work lists are compiled once per (layout, pass, partition) and cached.
 
 The Ring baseline (`mode='ring'`, src/onereel/parallel/ring.py) runs on the same kernels (onereel_b200/ring.py).
-Frame memory (`frame_memory`, onereel_b200/frame_memory.py) plugs in through install_attention's hooks. Variants the
-reference also carries but that are not on this path (bounded memory `memory`, `subject_links`) raise
-NotImplementedError here; `shared_pos='adjacent'` likewise.
+Frame memory (`frame_memory`, onereel_b200/frame_memory.py) plugs in through install_attention's hooks;
+`shared_pos='adjacent'` re-rotates the shared-frame keys inside the packed K (orl_rope_rows) and `scene_rope`
+restarts the temporal RoPE index per scene. Variants the reference also carries but that are not on this path
+(bounded memory `memory`, `subject_links`) raise NotImplementedError here.
 """
 from __future__ import annotations
 
@@ -23,7 +24,7 @@ from onereel_b200 import attention as A
 from onereel_b200 import comm, dist as D, ring as R
 from onereel_b200 import scene as S
 from onereel_b200.layout import SceneLayout
-from onereel_b200.rope import qk_norm_rope
+from onereel_b200.rope import qk_norm_rope, rotate_rows
 
 
 @dataclass
@@ -82,8 +83,94 @@ def _layout_key(lay: SceneLayout):
 def _unsupported(ctx):
     if ctx.memory or ctx.subject_links:
         raise NotImplementedError('bounded memory and subject links are not on the B200 path')
-    if ctx.shared_pos == 'adjacent' or (ctx.shared_pos == 'switch' and ctx.step() >= ctx.shared_switch):
-        raise NotImplementedError("shared_pos='adjacent' (shared-key RoPE re-rotation) is not on the B200 path")
+
+
+def _move_active(ctx) -> bool:
+    """hunyuan15.py:162: shared keys re-rotated to adjacent positions in this forward"""
+    return ctx.shared_pos == 'adjacent' or (ctx.shared_pos == 'switch' and ctx.step() >= ctx.shared_switch)
+
+
+def adjacent_positions(lay, j: int) -> list[int]:
+    """hunyuan15.py:92-100: per shared frame of scene j (shared_frames order) its temporal position — the shared
+    frames before the scene just before its first frame, those after it just after its last"""
+    lo, hi = lay.ranges[j]
+    shared = lay.shared_frames(j)
+    before = sorted(f for f in shared if f < lo)
+    after = sorted(f for f in shared if f >= hi)
+    pos = {f: lo - len(before) + i for i, f in enumerate(before)}
+    pos.update({f: hi + i for i, f in enumerate(after)})
+    return [pos[f] for f in shared]
+
+
+def frame_position(ctx, f: int) -> int:
+    """hunyuan15.py:103-113: temporal RoPE index of latent frame f (with scene_rope: index within its scene, + 1
+    after scene 0)"""
+    if not ctx.scene_rope:
+        return f
+    start = 0
+    for n in list(ctx.rope_lengths or ctx.layout.lengths):
+        if f < start + n:
+            return f - start + (start > 0)
+        start += n
+    raise IndexError(f)
+
+
+def shared_positions(ctx, j: int) -> list[int]:
+    """hunyuan15.py:116-124: per shared frame of scene j, its temporal RoPE index under shared_pos = 'adjacent'"""
+    lay = ctx.layout
+    if not ctx.scene_rope:
+        return adjacent_positions(lay, j)
+    shared = lay.shared_frames(j)
+    last = max(frame_position(ctx, f) for f in lay.frames[j])
+    pos = {f: last + 1 + i for i, f in enumerate(sorted(shared))}
+    return [pos[f] for f in shared]
+
+
+def scene_rope_rows(ctx, device):
+    """hunyuan15.py:443-454: per video token row, the rotary row of the same spatial position at its frame index
+    within its scene (+ 1 after scene 0)"""
+    lengths = list(ctx.rope_lengths or ctx.layout.lengths)
+    key = ('scene_rope', tuple(lengths), ctx.T)
+    if key not in ctx._cache:
+        start = np.repeat(np.cumsum([0] + lengths[:-1]), lengths)
+        local = np.arange(sum(lengths)) - start + (start > 0)
+        rows = (local[:, None] * ctx.T + np.arange(ctx.T)[None]).reshape(-1)
+        ctx._cache[key] = torch.as_tensor(rows, device=device)
+    return ctx._cache[key]
+
+
+def _shared_rotation(ctx, plan, device):
+    """hunyuan15.py:127-150 `_move_shared` as one rotation per row: for every video segment of `plan`, the packed K
+    rows of its shared frames and the tables of R(dst) R(src)^-1 (the two rotary rows a, a + d of the reference,
+    composed: cos(b - a), sin(b - a)); None when no segment has shared frames"""
+    cos, sin = ctx._rot_full
+    key = ('move', id(plan), cos.data_ptr(), sin.data_ptr())
+    if key in ctx._cache:
+        return ctx._cache[key]
+    lay, T = ctx.layout, ctx.T
+    rows, a_rows, b_rows = [], [], []
+    for i, sg in enumerate(plan.segs):
+        if sg.kind != 'v':
+            continue
+        shared = lay.shared_frames(sg.scene)
+        if not shared:
+            continue
+        base = plan.cu_k[i] + len(lay.frames[sg.scene]) * T
+        rows.append(torch.arange(base, base + len(shared) * T))
+        for f, dst in zip(shared, shared_positions(ctx, sg.scene)):
+            d = dst - frame_position(ctx, f)
+            a = 0 if d >= 0 else -d
+            a_rows.append(torch.arange(a * T, (a + 1) * T))
+            b_rows.append(torch.arange((a + d) * T, (a + d + 1) * T))
+    if not rows:
+        ctx._cache[key] = None
+        return None
+    ar, br = torch.cat(a_rows).to(cos.device), torch.cat(b_rows).to(cos.device)
+    ca, sa, cb, sb = (t.float() for t in (cos[ar], sin[ar], cos[br], sin[br]))
+    res = (torch.cat(rows).to(device=device, dtype=torch.int32),
+           (cb * ca + sb * sa).contiguous(), (sb * ca - cb * sa).contiguous())
+    ctx._cache[key] = res
+    return res
 
 
 class _RankPlan:
@@ -113,10 +200,14 @@ class _RankPlan:
             self.far_local = self.far_remote = None
 
 
-def _attend(plan, q, eq, k, v, ek, ev, ov, ot, rk=None, rv=None, lse_v=None, lse_t=None):
+def _attend(plan, q, eq, k, v, ek, ev, ov, ot, rk=None, rv=None, lse_v=None, lse_t=None, ctx=None):
     if plan is None or not plan.segs:
         return
     kp, vp = plan.pack_kv(k, v, ek, ev, rk, rv)
+    if ctx is not None and _move_active(ctx):
+        rot = _shared_rotation(ctx, plan, kp.device)
+        if rot is not None:
+            rotate_rows(kp, *rot)
     S.attend_segments(plan, q, eq, kp, vp, ov, ot, lse_v, lse_t)
 
 
@@ -133,6 +224,8 @@ class Processor:
         cos, sin = image_rotary_emb
         ctx._rot_full = image_rotary_emb
         rows = local_rows(ctx)
+        if ctx.scene_rope:
+            rows = scene_rope_rows(ctx, cos.device)[rows]
         H = attn.heads
         # per-head RMSNorm + rotary embedding of the local rows in one fused kernel (orl_qk_norm_rope)
         q = qk_norm_rope(attn.to_q(hidden_states).to(torch.bfloat16), attn.norm_q.weight, cos[rows], sin[rows], H,
@@ -179,14 +272,17 @@ class Processor:
         ex = comm.HaloExchange(ctx.layout, ctx.own, ctx.T, k, v) if D.world() > 1 else None
         if ex is not None and ex.remote_index != plan.remote_index:
             raise RuntimeError('exchange layout differs from the compiled plan')
+        if _move_active(ctx) and plan.lse:
+            raise NotImplementedError("overlap='lse' with shared_pos='adjacent' is not on the B200 path")
         ov, ot = torch.empty_like(q), torch.zeros_like(eq)
-        _attend(plan.near, q, eq, k, v, ek, ev, ov, ot)
+        _attend(plan.near, q, eq, k, v, ek, ev, ov, ot, ctx=ctx)
         if plan.lse:
             self._far_lse(plan, ex, q, eq, k, v, ek, ev, ov, ot)
         else:
             if ex is not None:
                 ex.wait()
-            _attend(plan.far, q, eq, k, v, ek, ev, ov, ot, ex.remote_k if ex else None, ex.remote_v if ex else None)
+            _attend(plan.far, q, eq, k, v, ek, ev, ov, ot, ex.remote_k if ex else None, ex.remote_v if ex else None,
+                    ctx=ctx)
         if ctx.text_sync == 'all_reduce' or D.world() == 1:
             D.all_reduce(ot)
         else:
@@ -243,7 +339,7 @@ class Processor:
                 Hl * Dh * 2, Hl, q.device)
         ov = torch.empty_like(qa)
         otl = torch.zeros_like(eqs)
-        _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl)
+        _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl, ctx=ctx)
         ot = eq.new_zeros(eq.shape)
         ot[:, sl] = otl
         D.all_reduce(ot)

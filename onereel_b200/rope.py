@@ -32,3 +32,16 @@ def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: 
                                      None if rm is None else rm.data_ptr(),
                                      torch.cuda.current_stream(x.device).cuda_stream), 'orl_qk_norm_rope')
     return out
+
+
+def rotate_rows(x: torch.Tensor, rows: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, sin_shift: int = 0):
+    """in place: rows `rows` (int32 CUDA tensor) of x [N, H, D] bf16 rotated by the table rows cos / sin
+    [len(rows), D] fp32 (orl_rope_rows)"""
+    Nr = rows.numel()
+    if Nr == 0:
+        return x
+    H, Dh = x.shape[1:]
+    L.check(L.lib().orl_rope_rows(x.data_ptr(), rows.data_ptr(), Nr, H, Dh, cos.data_ptr(), sin.data_ptr(),
+                                  cos.shape[1], int(sin_shift), torch.cuda.current_stream(x.device).cuda_stream),
+            'orl_rope_rows')
+    return x
