@@ -8,10 +8,11 @@
 //   warp 0      TMA producer: Q tiles once, then K_j / V_j tiles of 128 rows into a ring of shared-memory stages
 //   warp 1      TMEM owner and MMA issuer (one elected thread): S_t = Q_t K_j^T (SS form), O_t += P_t V_j (TS form,
 //               P read from TMEM in two 64-key halves), each committed to an mbarrier
-//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: thread = query row = TMEM lane. Loads the S row,
+//   warps 4-11  softmax, all eight on one tile at a time (tile 0, then tile 1, per 128-key step): a warp owns 16
+//               TMEM lanes (query rows), a quad of threads one row, 32 of its 128 scores per thread. Loads S,
 //               exponentiates against the running max while reducing the tile max (rescaling O in TMEM only when
-//               the max jumps by more than 2^64), writes P (bf16) over its S columns, then normalises O and stores
-//               the bf16 row and its LSE.
+//               the max jumps by more than 2^64), writes P (bf16) over the S columns, then normalises O and stores
+//               the bf16 rows and their LSE.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 [256+D,256+2D).
 // Warpgroup 0 runs on kRegsLow registers per thread and the softmax warpgroups on kRegsHigh (setmaxnreg).
 // Every mbarrier wait is bounded (ptx.cuh kWaitLimitNs): a stuck pipeline sets the error word and winds down.
@@ -61,7 +62,7 @@ struct AttnCfg {
 constexpr int kThreads = 384;
 // register split: the launch has 384 threads x 168 registers; warpgroup 0 (producer, MMA issuer, two idle warps)
 // keeps kRegsLow, the two softmax warpgroups get kRegsHigh (4 x 32 x kRegsLow + 8 x 32 x kRegsHigh = 384 x 168)
-constexpr int kLaunchRegs = 168, kRegsLow = 88, kRegsHigh = 208;
+constexpr int kLaunchRegs = 168, kRegsLow = 120, kRegsHigh = 192;
 static_assert(4 * kRegsLow + 8 * kRegsHigh == 12 * kLaunchRegs, "register split must add up to the launch total");
 // The softmax exponentiates against the running max it already has and computes the tile's max alongside; only
 // when a score exceeds that max by more than 2^kMaxJump (in exp2 units) is the tile redone against the new max and
@@ -201,148 +202,181 @@ __device__ __forceinline__ void mma_role(const AttnShared& sh, uint32_t tmem, in
 }
 
 // ---------------------------------------------------------------------------------------------- softmax
-// One thread per query row (= TMEM lane) of tile t. Per 128-key tile: load the S row, mask keys past the segment,
-// exponentiate against the running max while reducing the tile's max alongside (the first tile takes its max first);
-// if the tile's max exceeds the running one by more than kMaxJump (exp2 units) the warp redoes the tile against the
-// new max and rescales its O rows in TMEM (PV of the previous tile has completed: S of this tile was issued after
-// it). P (bf16) goes over the S columns in two halves, each handed to the MMA warp as soon as it is stored.
+__device__ __forceinline__ float quad_max(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+}
+__device__ __forceinline__ float quad_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  return x + __shfl_xor_sync(0xffffffffu, x, 2);
+}
+
+// All eight softmax warps work on one query tile at a time (tile 0, then tile 1, per 128-key step), so each tile's
+// softmax — the link between its S MMA and its PV MMA — takes half as long as with one warpgroup per tile. Warp sw
+// (0..7) owns TMEM lanes 32 (sw % 4) + 16 (sw / 4) + [0, 16); each thread holds two rows (lanes l/4, l/4 + 8 of that
+// block) and 32 of their 128 scores, a quad of threads shares a row (row max by two shuffles; row sums stay per
+// thread until the end). Per 128-key tile: exponentiate against the running max while reducing the tile's max
+// alongside (the first tile takes its max first); if the tile's max exceeds the running one by more than kMaxJump
+// (exp2 units) the rows are redone against the new max and their O rescaled in TMEM (PV of the previous tile has
+// completed: S of this tile was issued after it). P (bf16) goes over the S columns in two 64-key halves, each handed
+// to the MMA warp as soon as all eight warps stored it.
 template <int D>
-__device__ __forceinline__ void softmax_role(const AttnShared& sh, uint32_t tmem, int t, int quad, int lane,
-                                             const AttnWork& wi, int n_kv, float scale_log2,
+__device__ __forceinline__ void softmax_role(const AttnShared& sh, uint32_t tmem, int sw, int lane,
+                                             const AttnWork& wi, int n_qt, int n_kv, float scale_log2,
                                              __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
                                              long long nq_total, int heads, int* err) {
   using C = AttnCfg<D>;
-  const int row = 32 * quad + lane;
-  const int item_row = 128 * t + row;
-  const uint32_t lane_off = static_cast<uint32_t>(32 * quad) << 16;
-  const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
-  const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
-  const bool row_valid = item_row < wi.q_len;
-  __nv_bfloat16* orow = out + (static_cast<long long>(wi.q_row0) + item_row) * heads * D + wi.head * D;
-  float m_run = -INFINITY, l_run = 0.f;
+  const int cq = lane & 3;
+  const int lrow = 32 * (sw & 3) + 16 * (sw >> 2) + (lane >> 2);     // tile row of the first of the two rows
+  const uint32_t lane_off = static_cast<uint32_t>(32 * (sw & 3) + 16 * (sw >> 2)) << 16;
+  float m_run[2][2] = {{-INFINITY, -INFINITY}, {-INFINITY, -INFINITY}};
+  float l_run[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   bool ok = n_kv > 0;
   for (int j = 0; ok && j < n_kv; ++j) {
-    ok = mbar_wait(sh.bar(C::kBarS + t), j & 1, sh.abort_flag);
-    if (!ok) break;
-    tc_fence_after();
-    uint32_t r[4][32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, r[c]);
-    tmem_wait_ld();
     const int valid = wi.k_len - 128 * j;
-    if (valid < 128) {
+    for (int t = 0; t < n_qt; ++t) {
+      ok = mbar_wait(sh.bar(C::kBarS + t), j & 1, sh.abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
+      uint32_t s[64];                          // s[4r + 2i + e]: row i, key 8r + 2 cq + e
+      tmem_ld_16x256b_x8(s_addr, s);
+      tmem_ld_16x256b_x8(s_addr + 64, s + 32);
+      tmem_wait_ld();
+      if (valid < 128) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int r = 0; r < 16; ++r)
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (32 * c + e >= valid) r[c][e] = __float_as_uint(-INFINITY);
-    }
-    auto row_max = [&]() {
-      float m0 = __uint_as_float(r[0][0]), m1 = __uint_as_float(r[1][0]);
-      float m2 = __uint_as_float(r[2][0]), m3 = __uint_as_float(r[3][0]);
-#pragma unroll
-      for (int e = 1; e < 31; e += 2) {
-        m0 = fmax3(m0, __uint_as_float(r[0][e]), __uint_as_float(r[0][e + 1]));
-        m1 = fmax3(m1, __uint_as_float(r[1][e]), __uint_as_float(r[1][e + 1]));
-        m2 = fmax3(m2, __uint_as_float(r[2][e]), __uint_as_float(r[2][e + 1]));
-        m3 = fmax3(m3, __uint_as_float(r[3][e]), __uint_as_float(r[3][e + 1]));
+          for (int k = 0; k < 4; ++k)
+            if (8 * r + 2 * cq + (k & 1) >= valid) s[4 * r + k] = __float_as_uint(-INFINITY);
       }
-      return fmaxf(fmax3(m0, m1, __uint_as_float(r[0][31])),
-                   fmax3(m2, m3, fmax3(__uint_as_float(r[1][31]), __uint_as_float(r[2][31]),
-                                       __uint_as_float(r[3][31]))));
-    };
-    // exponentials of columns [64 half, 64 half + 64) against -m * log2e * scale = neg: packed bf16 P, sum
-    auto exp_half = [&](int half, float neg, uint32_t (&p)[32]) {
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+      auto tile_max = [&](int i) {
+        float a = __uint_as_float(s[2 * i]), b = __uint_as_float(s[2 * i + 1]);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int c = 2 * half + (e >> 4);
-        const int k = (2 * e) & 31;
-        const float p0 = ex2(fmaf(__uint_as_float(r[c][k]), scale_log2, neg));
-        const float p1 = ex2(fmaf(__uint_as_float(r[c][k + 1]), scale_log2, neg));
-        if (e & 1) {
-          s2 += p0;
-          s3 += p1;
-        } else {
-          s0 += p0;
-          s1 += p1;
+        for (int r = 1; r < 16; r += 2) {
+          a = fmax3(a, __uint_as_float(s[4 * r + 2 * i]), __uint_as_float(s[4 * r + 2 * i + 1]));
+          if (r + 1 < 16) b = fmax3(b, __uint_as_float(s[4 * (r + 1) + 2 * i]), __uint_as_float(s[4 * (r + 1) + 2 * i + 1]));
         }
-        p[e] = pack_bf16x2(p0, p1);
-      }
-      return (s0 + s1) + (s2 + s3);
-    };
-    float m_use = m_run;
-    bool redo = false;
-    uint32_t pa[32];
-    float sum;
-    if (j == 0) {
-      m_use = row_max();
-      sum = exp_half(0, -m_use * scale_log2, pa);
-    } else {
-      sum = exp_half(0, -m_run * scale_log2, pa);       // speculative: the max is reduced alongside
-      const float mx = row_max();
-      redo = (mx - m_run) * scale_log2 > kMaxJump;
-      if (__any_sync(0xffffffffu, redo)) {
-        m_use = fmaxf(m_run, mx);
-        const float alpha = ex2((m_run - m_use) * scale_log2);
-        sum = exp_half(0, -m_use * scale_log2, pa);
-        l_run *= alpha;
+        return quad_max(fmaxf(a, b));
+      };
+      // exponentials of keys [64 h, 64 h + 64) of both rows against neg_i = -m_i * log2e * scale: P words for a
+      // 16x128b store (register 2r + i: row i, word 4r + cq) and the two rows' sums
+      auto exp_half = [&](int h, float neg0, float neg1, uint32_t (&p)[16], float& sum0, float& sum1) {
+        float a0 = 0.f, b0 = 0.f, a1 = 0.f, b1 = 0.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + 32 * c, o);
-          tmem_wait_ld();
+        for (int r = 0; r < 8; ++r) {
+          const int base = 4 * (8 * h + r);
+          const float x0 = ex2(fmaf(__uint_as_float(s[base + 0]), scale_log2, neg0));
+          const float x1 = ex2(fmaf(__uint_as_float(s[base + 1]), scale_log2, neg0));
+          const float y0 = ex2(fmaf(__uint_as_float(s[base + 2]), scale_log2, neg1));
+          const float y1 = ex2(fmaf(__uint_as_float(s[base + 3]), scale_log2, neg1));
+          a0 += x0;
+          b0 += x1;
+          a1 += y0;
+          b1 += y1;
+          p[2 * r + 0] = pack_bf16x2(x0, x1);
+          p[2 * r + 1] = pack_bf16x2(y0, y1);
+        }
+        sum0 = a0 + b0;
+        sum1 = a1 + b1;
+      };
+      float* mr = m_run[t];
+      float* lr = l_run[t];
+      float m_use0 = mr[0], m_use1 = mr[1];
+      uint32_t pa[16];
+      float sa0, sa1;
+      if (j == 0) {
+        m_use0 = tile_max(0);
+        m_use1 = tile_max(1);
+        exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
+      } else {
+        exp_half(0, -mr[0] * scale_log2, -mr[1] * scale_log2, pa, sa0, sa1);   // speculative
+        const float mx0 = tile_max(0), mx1 = tile_max(1);
+        const bool redo = (mx0 - mr[0]) * scale_log2 > kMaxJump || (mx1 - mr[1]) * scale_log2 > kMaxJump;
+        if (__any_sync(0xffffffffu, redo)) {
+          m_use0 = fmaxf(mr[0], mx0);
+          m_use1 = fmaxf(mr[1], mx1);
+          const float al0 = ex2((mr[0] - m_use0) * scale_log2), al1 = ex2((mr[1] - m_use1) * scale_log2);
+          exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
+          lr[0] *= al0;
+          lr[1] *= al1;
+          const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_addr + 32 * c, o);
+          for (int ch = 0; ch < D / 64; ++ch) {
+            uint32_t o[32];
+            tmem_ld_16x256b_x8(o_addr + 64 * ch, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * ((e & 2) ? al1 : al0));
+            tmem_st_16x256b_x8(o_addr + 64 * ch, o);
+          }
         }
       }
+      tmem_st_16x128b_x8(s_addr, pa);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(sh.bar(C::kBarP + 2 * t + 0));
+      uint32_t pb[16];
+      float sb0, sb1;
+      exp_half(1, -m_use0 * scale_log2, -m_use1 * scale_log2, pb, sb0, sb1);
+      tmem_st_16x128b_x8(s_addr + 32, pb);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(sh.bar(C::kBarP + 2 * t + 1));
+      lr[0] += sa0 + sb0;
+      lr[1] += sa1 + sb1;
+      mr[0] = m_use0;
+      mr[1] = m_use1;
     }
-    tmem_st32(s_addr, pa);
-    tmem_wait_st();
-    tc_fence_before();
-    mbar_arrive(sh.bar(C::kBarP + 2 * t + 0));
-    uint32_t pb[32];
-    sum += exp_half(1, -m_use * scale_log2, pb);
-    tmem_st32(s_addr + 32, pb);
-    tmem_wait_st();
-    tc_fence_before();
-    mbar_arrive(sh.bar(C::kBarP + 2 * t + 1));
-    l_run += sum;
-    m_run = m_use;
   }
   if (ok) ok = mbar_wait(sh.bar(C::kBarDone), 0, sh.abort_flag);
   if (ok) {
     tc_fence_after();
-    const float inv = 1.0f / l_run;
+    for (int t = 0; t < n_qt; ++t) {
+      const float l0 = quad_sum(l_run[t][0]), l1 = quad_sum(l_run[t][1]);
+      const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+      const int r0 = 128 * t + lrow, r1 = r0 + 8;
+      const bool v0 = r0 < wi.q_len, v1 = r1 < wi.q_len;
+      __nv_bfloat16* o0 = out + (static_cast<long long>(wi.q_row0) + r0) * heads * D + wi.head * D + 2 * cq;
+      __nv_bfloat16* o1 = o0 + 8ll * heads * D;
+      const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
 #pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t o[32];
-      tmem_ld32(o_addr + 32 * c, o);
-      tmem_wait_ld();
-      if (row_valid) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+      for (int ch = 0; ch < D / 64; ++ch) {
+        uint32_t o[32];
+        tmem_ld_16x256b_x8(o_addr + 64 * ch, o);
+        tmem_wait_ld();
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-          dst[v] = w;
+        for (int r = 0; r < 8; ++r) {
+          const int col = 64 * ch + 8 * r;
+          if (v0)
+            *reinterpret_cast<uint32_t*>(o0 + col) =
+                pack_bf16x2(__uint_as_float(o[4 * r + 0]) * inv0, __uint_as_float(o[4 * r + 1]) * inv0);
+          if (v1)
+            *reinterpret_cast<uint32_t*>(o1 + col) =
+                pack_bf16x2(__uint_as_float(o[4 * r + 2]) * inv1, __uint_as_float(o[4 * r + 3]) * inv1);
         }
       }
+      if (lse != nullptr && cq == 0) {
+        const long long lb = static_cast<long long>(wi.head) * nq_total + wi.q_row0;
+        if (v0) lse[lb + r0] = (m_run[t][0] * scale_log2 + lg2(l0)) * 0.69314718055994530942f;
+        if (v1) lse[lb + r1] = (m_run[t][1] * scale_log2 + lg2(l1)) * 0.69314718055994530942f;
+      }
     }
-    if (lse != nullptr && row_valid)
-      lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] =
-          (m_run * scale_log2 + lg2(l_run)) * 0.69314718055994530942f;
   } else if (n_kv > 0) {
     atomicOr(err, kErrTimeoutSoftmax);
-  } else if (row_valid) {
+  } else {
     // a segment without keys: zero output, LSE -inf
-    uint4* dst = reinterpret_cast<uint4*>(orow);
-    for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
-    if (lse != nullptr) lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + item_row] = -INFINITY;
+    for (int t = 0; t < n_qt; ++t) {
+      const int r0 = 128 * t + lrow;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int rr = r0 + 8 * i;
+        if (rr >= wi.q_len) continue;
+        __nv_bfloat16* orow = out + (static_cast<long long>(wi.q_row0) + rr) * heads * D + wi.head * D + 2 * cq;
+        for (int col = 0; col < D; col += 8) *reinterpret_cast<uint32_t*>(orow + col) = 0u;
+        if (lse != nullptr && cq == 0) lse[static_cast<long long>(wi.head) * nq_total + wi.q_row0 + rr] = -INFINITY;
+      }
+    }
   }
 }
 
@@ -375,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(sh.bar(C::kBarE + s), 1);
     }
     for (int t = 0; t < 2; ++t) mbar_init(sh.bar(C::kBarS + t), 1);
-    for (int i = 0; i < 4; ++i) mbar_init(sh.bar(C::kBarP + i), 128);
+    for (int i = 0; i < 4; ++i) mbar_init(sh.bar(C::kBarP + i), 256);
     mbar_init(sh.bar(C::kBarDone), 1);
     mbar_init(sh.bar(C::kBarDrain), 1);
     *sh.abort_flag = 0;
@@ -400,8 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     regs_inc<kRegsHigh>();
-    const int t = (warp - 4) >> 2;
-    if (t < n_qt) softmax_role<D>(sh, tmem, t, warp & 3, lane, wi, n_kv, scale_log2, out, lse, nq_total, heads, err);
+    softmax_role<D>(sh, tmem, warp - 4, lane, wi, n_qt, n_kv, scale_log2, out, lse, nq_total, heads, err);
   }
 
   tc_fence_before();
