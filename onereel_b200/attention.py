@@ -120,6 +120,20 @@ def attend(q, k, v, q_start, q_len, k_start, k_len, out=None, lse=None, scale=No
     return out, lse
 
 
+def attend_work(q, k, v, work, n_items: int, out, lse=None, scale=None, stream=None):
+    """the kernel call with a caller-held device work list (orl_attn_plan_ranges items, possibly edited on the
+    device since: the bounded memory sets each item's key count per head from its selection)"""
+    _check_inputs(q, k, v)
+    Nq, H, Dh = q.shape
+    dev = q.device
+    scale = Dh ** -0.5 if scale is None else float(scale)
+    s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    L.check(L.lib().orl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                 None if lse is None else lse.data_ptr(), Nq, k.shape[0], H, Dh, scale,
+                                 work.data_ptr(), n_items, _err_word(dev).data_ptr(), s), 'orl_attn_fwd')
+    return out
+
+
 def _cu_to_ranges(cu_q, cu_k):
     cq, ck = _host_list(cu_q), _host_list(cu_k)
     if len(cq) != len(ck):

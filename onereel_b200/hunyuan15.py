@@ -10,8 +10,9 @@ all local. The segment list, run tables and work lists are compiled once per (la
 The Ring baseline (`mode='ring'`, src/onereel/parallel/ring.py) runs on the same kernels (onereel_b200/ring.py).
 Frame memory (`frame_memory`, onereel_b200/frame_memory.py) plugs in through install_attention's hooks;
 `shared_pos='adjacent'` re-rotates the shared-frame keys inside the packed K (orl_rope_rows) and `scene_rope`
-restarts the temporal RoPE index per scene. Variants the reference also carries but that are not on this path
-(bounded memory `memory`, `subject_links`) raise NotImplementedError here.
+restarts the temporal RoPE index per scene. The bounded cross-scene memory (`memory` = M, onereel_b200/memory.py)
+runs on one GPU, on Ulysses and on the gathering path. `subject_links`, a variant the reference also carries, is not
+on this path and raises NotImplementedError.
 """
 from __future__ import annotations
 
@@ -22,6 +23,7 @@ import torch
 
 from onereel_b200 import attention as A
 from onereel_b200 import comm, dist as D, ring as R
+from onereel_b200 import memory as MEM
 from onereel_b200 import scene as S
 from onereel_b200.layout import SceneLayout
 from onereel_b200.rope import qk_norm_rope, rotate_rows
@@ -81,8 +83,8 @@ def _layout_key(lay: SceneLayout):
 
 
 def _unsupported(ctx):
-    if ctx.memory or ctx.subject_links:
-        raise NotImplementedError('bounded memory and subject links are not on the B200 path')
+    if ctx.subject_links:
+        raise NotImplementedError('subject links are not on the B200 path')
 
 
 def _move_active(ctx) -> bool:
@@ -240,7 +242,9 @@ class Processor:
         if getattr(attn, 'norm_added_k', None) is not None:
             ek = attn.norm_added_k(ek)
         eq, ek, ev = (x[0].to(torch.bfloat16).contiguous() for x in (eq, ek, ev))
-        if ctx.run_mode == 'ulysses' or ctx.attn_override is not None:
+        if ctx.memory:
+            hs, ehs = self.memory(q, k, v, eq, ek, ev)
+        elif ctx.run_mode == 'ulysses' or ctx.attn_override is not None:
             hs, ehs = self.ulysses(q, k, v, eq, ek, ev)
         elif ctx.run_mode == 'ring':
             hs, ehs = R.attention(ctx.ring, q, k, v, eq, ek, ev, ctx.text_ranges(), id(ctx.layout.extra))
@@ -249,6 +253,52 @@ class Processor:
         hs = attn.to_out[1](attn.to_out[0](hs.flatten(1, 2)[None].to(hidden_states.dtype)))
         ehs = attn.to_add_out(ehs.flatten(1, 2)[None].to(hidden_states.dtype))
         return hs, ehs
+
+    def memory(self, q, k, v, eq, ek, ev):
+        """hunyuan15.py:305-333: bounded cross-scene memory (onereel_b200.memory). One GPU or Ulysses: all tokens of
+        the local heads, each rank clusters its own heads. K/V gathering: the rank's scene pieces read their scenes
+        (split scenes completed from the peers) and every boundary candidate (received from its owner); every rank
+        clusters the same candidates, so all agree on the representatives without exchanging them."""
+        ctx, T, lay = self.ctx, self.ctx.T, self.ctx.layout
+        if ctx._mem is None:
+            ctx._mem = MEM.MemoryAttention(MEM.BoundaryMemory(ctx.memory))
+        key, counts = (self.layer, ctx.cond()), ctx.counts[ctx.cond()]
+        n, r, H = D.world(), D.rank(), q.shape[1]
+        eq_full = eq
+        rk = rv = None
+        if ctx.run_mode == 'ulysses' or n == 1:
+            sl = slice(r * H // n, (r + 1) * H // n)
+            if n > 1:
+                q, k, v = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
+                eq, ek, ev = (x[:, sl].contiguous() for x in (eq, ek, ev))
+            own, remote_index = (0, lay.n_frames * T), []
+            scenes = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
+            text_for = set(range(lay.n_scenes))
+        else:
+            sl = slice(None)
+            own = tuple(ctx.own[r])
+            ex = comm.HaloExchange(lay, ctx.own, T, k, v, extra=MEM.candidate_frames(lay)[0])
+            ex.wait()
+            remote_index, rk, rv = ex.remote_index, ex.remote_k, ex.remote_v
+            scenes, text_for = S.pieces(lay, T, own)
+        Hl, Dh = q.shape[1:]
+        pk = (_layout_key(lay), T, tuple(counts), own, tuple(map(tuple, remote_index)), Hl, Dh, str(q.device))
+        plan = ctx._mem.plans.get(pk)
+        if plan is None:
+            plan = ctx._mem.plans[pk] = MEM.MemoryPlan(lay, T, counts, own, remote_index, scenes, text_for, Hl, Dh,
+                                                       ctx.memory, q.device)
+        ov = torch.empty_like(q)
+        ot = torch.zeros_like(eq)
+        ctx._mem(key, plan, q, k, v, eq, ek, ev, ov, ot, rk, rv)
+        if n == 1:
+            return ov, ot
+        if sl != slice(None):
+            full = torch.zeros_like(eq_full)
+            full[:, sl] = ot
+            D.all_reduce(full)
+            return comm.a2a_tokens(ov), full
+        D.all_reduce(ot)
+        return ov, ot
 
     def _plan(self, H, Dh, device, lse_overlap):
         ctx = self.ctx
@@ -419,6 +469,12 @@ def install_attention(transformer, ctx: Context):
     counter and the frame-memory step / layer / pooling hooks; the token shard / gather hooks of the first / last block
     when parallel. `transformer` is the diffusers HunyuanVideo15Transformer3DModel (or any module with
     .transformer_blocks[i].attn.set_processor); blocks return (hidden states, text states)."""
+    if ctx.memory:
+        assert ctx.layout.halo == 0, 'the bounded memory replaces the halo frames: use halo = 0'
+        assert not ctx.subject_links, 'the bounded memory and subject links are separate variants'
+        ctx._mem = MEM.MemoryAttention(MEM.BoundaryMemory(ctx.memory))
+    if ctx.frame_memory is not None:
+        assert ctx.layout.halo == 0 and not ctx.memory, 'frame memory replaces the halo frames: use halo = 0'
     for i, blk in enumerate(transformer.transformer_blocks):
         blk.attn.set_processor(Processor(ctx, i))
 

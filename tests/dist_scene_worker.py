@@ -10,7 +10,10 @@ tests/dist_onereel_kv_chunks.py, dist_onereel_overlap.py, dist_onereel_gather.py
   - overlap='lse' (local keys during the exchange, LSE merge) within rel 1e-2 of waiting;
   - Ulysses equals the single-GPU result bit for bit; text_sync='all_reduce' equals 'rows' on touched scenes;
   - the Scene-Ring baseline (mode='ring', Hunyuan with text and Wan) within rel 1e-2 of the single-GPU result;
-  - the Eq. 2 chooser ('auto') picks a path and reproduces the single-GPU result.
+  - the Eq. 2 chooser ('auto') picks a path and reproduces the single-GPU result;
+  - the bounded memory (memory = 8, halo-free layouts): K/V gathering with the boundary candidates received equals
+    the single-GPU memory result bit for bit (every rank clusters the same candidates); Ulysses (each rank clusters
+    its own heads) within rel 2e-2.
 Prints PASS lines on rank 0; any failure raises (non-zero exit)."""
 import os
 import sys
@@ -104,6 +107,24 @@ def main():
         av, at = (HY.Processor(actx, 0).ulysses(*args) if actx.run_mode == 'ulysses'
                   else HY.Processor(actx, 0).scene(*args))
         assert torch.equal(av.contiguous(), ref_v[aa:ab]), (lengths, r, 'auto', actx.run_mode)
+        if halo == 0:
+            lay_m = SceneLayout(lengths, halo=0)
+            D.world, D.rank = (lambda: 1), (lambda: 0)
+            m1 = HY.Context(lay_m, T=T, own=[(0, L)], counts={True: counts}, fwd=1, memory=8)
+            mref_v, mref_t = HY.Processor(m1, 0).memory(q, k, v, eq, ek, ev)
+            D.world, D.rank = saved
+            mown = comm.partition(lay_m, n, T, 'scene', counts, 8)
+            ma, mb = mown[r]
+            mc = HY.Context(lay_m, T=T, own=mown, counts={True: counts}, fwd=1, memory=8)
+            mv, mt = HY.Processor(mc, 0).memory(*(x[ma:mb].contiguous() for x in (q, k, v)), eq, ek, ev)
+            assert torch.equal(mv, mref_v[ma:mb]), (lengths, r, 'memory gather video')
+            assert torch.equal(mt, mref_t), (lengths, r, 'memory gather text')
+            if L % n == 0 and H % n == 0:
+                uown = comm.partition(lay_m, n, T, 'ulysses')
+                ua, ub = uown[r]
+                muc = HY.Context(lay_m, T=T, own=uown, counts={True: counts}, fwd=1, memory=8, run_mode='ulysses')
+                muv, mut = HY.Processor(muc, 0).memory(*(x[ua:ub].contiguous() for x in (q, k, v)), eq, ek, ev)
+                assert rel(muv, mref_v[ua:ub]) < 2e-2 and rel(mut, mref_t) < 2e-2, (lengths, r, 'memory ulysses')
         torch.cuda.synchronize()
         A.check()
         if r == 0:

@@ -15,6 +15,10 @@ What is recorded (reference file:line in brackets):
                  tensors (video token t -> t, text row i -> -(i + 1)); the collectives are replaced by row lookups.
   frame_memory.json  FrameMemory selections and extra frames (src/onereel/frame_memory.py:24-132) on seeded features
   ring.json      RingPlan chunks / permutation / per-rank rows / key sets (src/onereel/parallel/ring.py:23-60)
+  memory.json    bounded memory (src/onereel/memory.py): candidate frames (31-38), BoundaryMemory.select (58-105) on
+                 seeded candidate keys — a first selection and a warm-started one — and the pieces of frame_plan
+                 (118-140) as built by hunyuan15.Processor.memory (305-333) at world 1 and per rank of gathering
+                 partitions (query rows and local key tokens of each piece)
   cfg1.npz       BASELINE cfg1 run through hunyuan15.Processor.scene at world 1 in fp32 on the CPU, with the FA varlen
                  call replaced by per-segment fp32 softmax attention: inputs are regenerated from seed 0 by the tests,
                  outputs stored as float32 (every 4th video row, every text row).
@@ -40,6 +44,7 @@ from onereel.models import hunyuan15 as HY, wan as WN         # noqa: E402
 from onereel.parallel import comm, dist as D                  # noqa: E402
 from onereel.parallel import ring as RG                       # noqa: E402
 from onereel.frame_memory import FrameMemory                  # noqa: E402
+from onereel import memory as MEMR                            # noqa: E402
 
 
 def rand_layout(rng, max_scenes=8, max_len=12):
@@ -322,9 +327,82 @@ def gen_frame_memory(rng):
     return out
 
 
+def gen_memory(rng):
+    """bounded memory: candidate_frames, select (init + warm-started update), frame_plan pieces"""
+    sel = []
+    for i in range(24):
+        lengths = [rng.randint(1, 6) for _ in range(rng.randint(1, 5))]
+        lay = SceneLayout(lengths, halo=0)
+        T, H, Dh = rng.choice([2, 4, 8]), rng.choice([1, 3]), rng.choice([8, 16, 32])
+        M = rng.choice([1, 3, 7, 12, 1000])
+        frames, owner = MEMR.candidate_frames(lay)
+        B = len(frames) * T
+        g = torch.Generator().manual_seed(500 + i)
+        kc = torch.randn(B, H, Dh, generator=g)
+        kc2 = kc + 0.3 * torch.randn(B, H, Dh, generator=g)
+        mem = MEMR.BoundaryMemory(M)
+        rep, valid = mem.select('k', kc)
+        rep2, valid2 = mem.select('k', kc2)
+        sel.append(dict(lengths=lengths, T=T, H=H, D=Dh, M=M, seed=500 + i, frames=frames, owner=owner,
+                        rep=rep.tolist(), valid=valid.tolist(), rep2=rep2.tolist(), valid2=valid2.tolist()))
+    plans = []
+    for i in range(16):
+        lengths = [rng.randint(1, 7) for _ in range(rng.randint(1, 6))]
+        lay = SceneLayout(lengths, halo=0)
+        T = rng.choice([2, 3, 4])
+        counts = [rng.randint(0, 5) for _ in lengths]
+        n = rng.choice([1, 2, 3, 4])
+        L_ = lay.n_frames * T
+        if L_ < 2 * n:
+            n = 1
+        own = comm.partition(lay, n, T, 'scene', counts, 8) if n > 1 else [(0, L_)]
+        tr, c = [], 0
+        for m in counts:
+            tr.append((c, c + m))
+            c += m
+        ranks = []
+        for r, (a, b) in enumerate(own):
+            cand = MEMR.candidate_frames(lay)[0]
+            if n == 1:
+                token_row = torch.arange(L_)
+                pieces = [(j, lo * T, hi * T) for j, (lo, hi) in enumerate(lay.ranges)]
+                text_for = set(range(lay.n_scenes))
+                Lv = L_
+            else:
+                need = comm.needed(lay, T, (a, b), cand)
+                held = [(a, b)] + [(lo, hi) for lo, hi in need]
+                token_row = torch.full((L_,), -1, dtype=torch.long)
+                row = 0
+                for lo, hi in held:
+                    token_row[lo:hi] = torch.arange(row, row + hi - lo)
+                    row += hi - lo
+                Lv = row
+                pieces = [(j, lo - a, hi - a) for j, (lo, hi) in
+                          [(j, (max(lo * T, a), min(hi * T, b))) for j, (lo, hi) in enumerate(lay.ranges)
+                           if lo * T < b and hi * T > a]]
+                text_for = {j for j, (lo, _) in enumerate(lay.ranges) if a <= lo * T < b}
+            Sq = (b - a) if n > 1 else L_
+            plan = MEMR.frame_plan(lay, T, token_row, Lv, pieces, tr, text_for, Sq, 'cpu')
+            inv = {int(rw): t for t, rw in enumerate(token_row.tolist()) if rw >= 0}
+            dec = lambda rw: inv[rw] if rw < Lv else -(rw - Lv + 1)
+            qoff = 0
+            out_pieces = []
+            for pi in range(len(plan.qlen)):
+                ql = int(plan.qlen[pi])
+                qr = plan.qrows[qoff:qoff + ql].tolist()
+                qoff += ql
+                keys = [dec(int(x)) for x in plan.pad[pi, :int(plan.lens[pi])].tolist()]
+                out_pieces.append(dict(scene=int(plan.scene[pi]), q=[qr[0], qr[-1] + 1], keys=keys,
+                                       mem=bool(plan.mem[pi])))
+            ranks.append(dict(own=[a, b], pieces=out_pieces, cand=[dec(int(x)) for x in plan.cand.tolist()]))
+        plans.append(dict(lengths=lengths, T=T, counts=counts, n=n, ranks=ranks))
+    return dict(select=sel, plans=plans)
+
+
 def main():
     (HERE / 'ring.json').write_text(json.dumps(gen_ring(random.Random(7))))
     (HERE / 'frame_memory.json').write_text(json.dumps(gen_frame_memory(random.Random(11))))
+    (HERE / 'memory.json').write_text(json.dumps(gen_memory(random.Random(13))))
     rng = random.Random(20261201)
     torch.set_num_threads(os.cpu_count())
     (HERE / 'layout.json').write_text(json.dumps(gen_layout(rng)))
