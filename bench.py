@@ -40,7 +40,7 @@ CFG4 = dict(lengths=[31, 31, 31, 31], T=1590, text=128, heads=16, dim=128, memor
             blocks=54, frame_hw=(30, 53))
 METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
 # DRAM bytes / algorithmic bytes of the attention kernel, from the small-case ncu capture (profiles/attn_fwd_cfg2.md)
-TRAFFIC_PER_ALG_BYTE = 376.64 / 392.9
+TRAFFIC_PER_ALG_BYTE = 373.86 / 392.9
 
 
 def cfg_layout(cfg):
