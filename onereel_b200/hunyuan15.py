@@ -285,11 +285,11 @@ class Processor:
         pk = (_layout_key(lay), T, tuple(counts), own, tuple(map(tuple, remote_index)), Hl, Dh, str(q.device))
         plan = ctx._mem.plans.get(pk)
         if plan is None:
-            plan = ctx._mem.plans[pk] = MEM.MemoryPlan(lay, T, counts, own, remote_index, scenes, text_for, Hl, Dh,
-                                                       ctx.memory, q.device)
+            plan = ctx._mem.plans[pk] = MEM.MemoryPlan.for_rank(lay, T, counts, own, remote_index, scenes, text_for,
+                                                                q.device)
         ov = torch.empty_like(q)
         ot = torch.zeros_like(eq)
-        ctx._mem(key, plan, q, k, v, eq, ek, ev, ov, ot, rk, rv)
+        ctx._mem.run(key, plan, q, k, v, eq, ek, ev, ov, ot, rk, rv)
         if n == 1:
             return ov, ot
         if sl != slice(None):

@@ -25,7 +25,7 @@ from onereel_b200 import _lib as L
 from onereel_b200 import attention as A
 from onereel_b200.layout import SceneLayout
 from onereel_b200.pack import RunTable
-from onereel_b200.scene import REMOTE, TEXT, VIDEO, scene_segments
+from onereel_b200.scene import TEXT, VIDEO, Segment, scene_segments
 
 ITERS_INIT, ITERS_UPDATE = 50, 2
 
@@ -104,38 +104,35 @@ class BoundaryMemory:
 
 
 class MemoryPlan:
-    """one rank's compiled memory call (memory.py:118-140 `make_plan` / `frame_plan`, B200 layout): the halo-free
-    scene segments of the rank's pieces (video segments read the memory, text segments do not), the packed K / V rows
-    (each video segment's local keys, then M' representative slots; one spare row at the end), the candidates'
-    sources, and the two launches' work lists (video queries in place from q, text queries from eq)."""
+    """one compiled memory call (memory.py:108-140 `Plan` / `make_plan` / `frame_plan`, B200 layout): the segments
+    (video segments read the memory, text segments do not), the candidates' sources and scenes; per (heads, head
+    dim), compiled on first use: the packed K / V rows (each video segment's local keys, then M' representative
+    slots; one spare row at the end), the pack run table and the two launches' work lists (video queries in place
+    from one source, text queries from the other)."""
 
-    def __init__(self, layout: SceneLayout, T: int, counts, own, remote_index, scenes, text_for, H: int, Dh: int,
-                 M: int, device):
-        self.H, self.Dh, self.device = H, Dh, torch.device(device)
+    def __init__(self, segs, cand_local, cand_remote, cand_owner, device):
+        """segs: scene.Segment list; cand_local / cand_remote: (candidate positions, source rows) in the local video
+        rows / the received buffer; cand_owner: the scene of every candidate (numpy)"""
+        self.segs, self.device = segs, torch.device(device)
+        self.B = len(cand_owner)
+        lt = lambda x: torch.as_tensor(np.asarray(x, dtype=np.int64), device=self.device)
+        self.cand_local_pos, self.cand_local_rows = lt(cand_local[0]), lt(cand_local[1])
+        self.cand_remote_pos, self.cand_remote_rows = lt(cand_remote[0]), lt(cand_remote[1])
+        self.cand_owner = lt(cand_owner)
+        self.vid = [i for i, sg in enumerate(segs) if sg.kind == 'v']
+        self.txt = [i for i, sg in enumerate(segs) if sg.kind == 't']
+        self.n_video = len(self.vid)
+        self.H = self.Dh = self.M = None
+        self.buffers = None
+
+    @classmethod
+    def for_rank(cls, layout: SceneLayout, T: int, counts, own, remote_index, scenes, text_for, device):
+        """the pieces of a rank owning video tokens own = (a, b) (hunyuan15.py:305-333 / wan.py:154-173): its scene
+        pieces with their scenes' own frames (halo-free) and sentence as local keys, the text segments of text_for;
+        candidates from the local rows or the received buffer (remote_index, which must cover them)"""
         plain = SceneLayout(layout.lengths, halo=0)             # local keys: the scene's own frames (memory.py:134)
-        self.segs = scene_segments(plain, T, counts, scenes, text_for, own, remote_index)
+        segs = scene_segments(plain, T, counts, scenes, text_for, own, remote_index)
         frames, owner = candidate_frames(layout)
-        self.B = len(frames) * T
-        self.M = min(M, self.B)
-        rb = H * Dh * 2
-        src_slot, dst_slot, src_off, dst_off, nbytes = [], [], [], [], []
-        row, self.base, self.n_local = 0, [], []
-        for s in self.segs:
-            self.base.append(row)
-            self.n_local.append(s.lk)
-            for src, lo, hi in s.kv:
-                src_slot.append(src)
-                dst_slot.append(3)
-                src_off.append(lo * rb)
-                dst_off.append(row * rb)
-                nbytes.append((hi - lo) * rb)
-                row += hi - lo
-            if s.kind == 'v':
-                row += self.M
-        self.spare = row
-        self.n_rows = row + 1
-        self.table = RunTable(src_slot, dst_slot, src_off, dst_off, nbytes, device)
-        # candidate k / v rows: from this rank's video rows or from the received exchange buffer
         a, b = own
         tokens = (np.asarray(frames)[:, None] * T + np.arange(T)[None]).reshape(-1)
         loc = (tokens >= a) & (tokens < b)
@@ -146,26 +143,44 @@ class MemoryPlan:
             if hit is None:
                 raise ValueError(f'candidate token {t} is neither local {own} nor received')
             rem_rows[i] = hit[2] + t - hit[0]
-        dev = self.device
-        lt = lambda v: torch.as_tensor(np.asarray(v, dtype=np.int64), device=dev)
-        self.cand_local_pos, self.cand_local_rows = lt(np.flatnonzero(loc)), lt(tokens[loc] - a)
-        self.cand_remote_pos, self.cand_remote_rows = lt(np.flatnonzero(~loc)), lt(rem_rows[~loc])
-        self.cand_owner = lt(np.repeat(owner, T))
-        # video segments: scene, packed base and local key count on the device (the per-head key counts are
-        # computed there every call); text segments: a static work list
-        vid = [i for i, s in enumerate(self.segs) if s.kind == 'v']
-        txt = [i for i, s in enumerate(self.segs) if s.kind == 't']
+        return cls(segs, (np.flatnonzero(loc), tokens[loc] - a), (np.flatnonzero(~loc), rem_rows[~loc]),
+                   np.repeat(owner, T), device)
+
+    def compile(self, H: int, Dh: int, M: int):
+        """packed row layout, run table and work lists for H heads of Dh and at most M representatives (once)"""
+        if self.H is not None:
+            assert (self.H, self.Dh, self.M) == (H, Dh, min(M, self.B)), 'a memory plan serves one head layout'
+            return
+        self.H, self.Dh, self.M = H, Dh, min(M, self.B)
+        self.base, self.n_local, row = [], [], 0
+        for sg in self.segs:
+            self.base.append(row)
+            self.n_local.append(sg.lk)
+            row += sg.lk + (self.M if sg.kind == 'v' else 0)
+        self.spare, self.n_rows = row, row + 1
+        lt = lambda x: torch.as_tensor(np.asarray(x, dtype=np.int64), device=self.device)
+        vid, txt = self.vid, self.txt
         self.v_scene = lt([self.segs[i].scene for i in vid])
         self.v_base = lt([self.base[i] for i in vid])
         self.v_local = lt([self.n_local[i] for i in vid])
-        self.n_video = len(vid)
+        rb = H * Dh * 2
+        src_slot, dst_slot, src_off, dst_off, nbytes = [], [], [], [], []
+        for i, sg in enumerate(self.segs):
+            row = self.base[i]
+            for src, lo, hi in sg.kv:
+                src_slot.append(src)
+                dst_slot.append(3)
+                src_off.append(lo * rb)
+                dst_off.append(row * rb)
+                nbytes.append((hi - lo) * rb)
+                row += hi - lo
+        self.table = RunTable(src_slot, dst_slot, src_off, dst_off, nbytes, self.device)
         self.v_work, self.v_items, self.v_key = self._work([self.segs[i].q[1] for i in vid],
                                                            [self.segs[i].lq for i in vid],
                                                            [self.base[i] for i in vid],
                                                            [self.n_local[i] + self.M for i in vid])
         self.t_q = ([self.segs[i].q[1] for i in txt], [self.segs[i].lq for i in txt],
                     [self.base[i] for i in txt], [self.n_local[i] for i in txt])
-        self.buffers = None
 
     def _work(self, qs, ql, ks, kl):
         """attention work list of the video segments with their largest key counts (the LPT order); per item, the
@@ -190,6 +205,37 @@ class MemoryPlan:
         return self.buffers
 
 
+def frame_plan(layout: SceneLayout, T: int, token_row, Lv: int, q_pieces, text_ranges=None, text_for=(), Sq: int = 0,
+               device='cuda') -> MemoryPlan:
+    """memory.py:118-140 with the reference's arguments: key buffer = Lv video rows (video token t at token_row[t])
+    then the text rows; query buffer = Sq video rows then the text rows; q_pieces [(scene, video query row lo, hi)].
+    Video queries read their scene's frames, their sentence and the memory; sentence queries (scenes in text_for)
+    their scene's frames and sentence. For MemoryAttention's reference-style call."""
+    token_row = np.asarray(torch.as_tensor(token_row).cpu(), dtype=np.int64)
+
+    def frame_runs(frames):
+        toks = np.concatenate([np.arange(f * T, (f + 1) * T) for f in frames]) if len(frames) else np.zeros(0, int)
+        rows = token_row[toks]
+        runs = []
+        for r in rows.tolist():
+            if runs and runs[-1][2] == r:
+                runs[-1] = (VIDEO, runs[-1][1], r + 1)
+            else:
+                runs.append((VIDEO, r, r + 1))
+        return runs
+    text = lambda j: ([(VIDEO, Lv + text_ranges[j][0], Lv + text_ranges[j][1])]
+                      if text_ranges and text_ranges[j][1] > text_ranges[j][0] else [])
+    segs = [Segment('v', j, (VIDEO, lo, hi), frame_runs(layout.frames[j]) + text(j), ('v', lo, hi))
+            for j, lo, hi in q_pieces if hi > lo]
+    segs += [Segment('t', j, (TEXT, Sq + text_ranges[j][0], Sq + text_ranges[j][1]),
+                     frame_runs(layout.frames[j]) + text(j), ('t', text_ranges[j][0], text_ranges[j][1]))
+             for j in sorted(text_for) if text_ranges and text_ranges[j][1] > text_ranges[j][0]]
+    frames, owner = candidate_frames(layout)
+    tokens = (np.asarray(frames)[:, None] * T + np.arange(T)[None]).reshape(-1)
+    return MemoryPlan(segs, (np.arange(len(tokens)), token_row[tokens]), (np.zeros(0, int), np.zeros(0, int)),
+                      np.repeat(owner, T), device)
+
+
 class MemoryAttention:
     """memory.py:143-174: scene attention with the bounded memory on the B200 kernels; plans are cached by the
     caller's key"""
@@ -198,12 +244,20 @@ class MemoryAttention:
         self.memory = memory
         self.plans = {}
 
+    def __call__(self, key, q, k, v, plan: MemoryPlan) -> torch.Tensor:
+        """the reference's call (memory.py:150-174): q [Sq, H, D] query buffer, k / v [L, H, D] key buffers laid out
+        as `frame_plan` describes -> [Sq, H, D] (rows outside the plan's queries are zero)"""
+        out = q.new_zeros(q.shape)
+        self.run(key, plan, q, k, v, q, k, v, out, out)
+        return out
+
     @torch.no_grad()
-    def __call__(self, key, plan: MemoryPlan, q, k, v, eq, ek, ev, ov, ot, remote_k=None, remote_v=None):
-        """q / k / v: this rank's video rows [rows, H, D] (bf16); eq / ek / ev: the text rows; remote_k / remote_v:
-        the received exchange buffers (gather path). Writes the video outputs into ov and the text outputs of the
-        plan's text segments into ot."""
-        H, Dh = plan.H, plan.Dh
+    def run(self, key, plan: MemoryPlan, q, k, v, eq, ek, ev, ov, ot, remote_k=None, remote_v=None):
+        """q / k / v: the video rows [rows, H, D] (bf16); eq / ek / ev: the text rows (or None); remote_k / remote_v:
+        the received exchange buffers (gather path). Writes the video segments' outputs into ov and the text
+        segments' into ot."""
+        H, Dh = q.shape[1:]
+        plan.compile(H, Dh, self.memory.M)
         dev = q.device
         kc = k.new_empty(plan.B, H, Dh)
         vc = v.new_empty(plan.B, H, Dh)
@@ -212,14 +266,14 @@ class MemoryAttention:
                 dst.index_copy_(0, plan.cand_local_pos, src.index_select(0, plan.cand_local_rows))
             if plan.cand_remote_pos.numel():
                 dst.index_copy_(0, plan.cand_remote_pos, r_src.index_select(0, plan.cand_remote_rows))
-        rep, valid = self.memory.select(key, kc)                                 # [H, M]
+        rep, valid = self.memory.select(key, kc)                                 # [H, M']
         kp, vp = plan.kv_buffers(q)
         ptr = lambda x: 0 if x is None else x.data_ptr()
         plan.table.run([ptr(k), ptr(ek), ptr(remote_k), 0, ptr(v), ptr(ev), ptr(remote_v), 0],
                        [0, 0, 0, kp.data_ptr(), 0, 0, 0, vp.data_ptr()], n_planes=2)
         if plan.n_video:
             foreign = valid[:, None, :] & (plan.cand_owner[rep][:, None, :] != plan.v_scene[None, :, None])
-            slot = foreign.cumsum(-1) - 1                                         # [H, n_video, M]
+            slot = foreign.cumsum(-1) - 1                                         # [H, n_video, M']
             dst = torch.where(foreign, (plan.v_base + plan.v_local)[None, :, None] + slot,
                               torch.full_like(slot, plan.spare))
             src = rep[:, None, :].expand_as(dst)

@@ -4,7 +4,8 @@ Context, 64-74 _qk, 77-173 Processor, 248-271 _plan_parallel).
 Self-attention has no joint text. One GPU / Ulysses: `ranges` — every scene's keys are one contiguous token range
 (scene plus adjacent halo), read in place by the attention kernel (orl_attn_plan_ranges: no copy), or packed per
 scene by the gather/pack kernel when the scene also reads frame-memory frames. K/V gathering: `scene`, as Hunyuan's
-without text. Cross-attention (per scene on its sentence) stays the model's own processor, as in the reference.
+without text. Bounded cross-scene memory (`memory` = M): `memory`, on onereel_b200/memory.py (one GPU, Ulysses, K/V
+gathering). Cross-attention (per scene on its sentence) stays the model's own processor, as in the reference.
 """
 from __future__ import annotations
 
@@ -15,6 +16,7 @@ import torch.nn.functional as F
 
 from onereel_b200 import attention as A
 from onereel_b200 import comm, dist as D, ring as R
+from onereel_b200 import memory as MEM
 from onereel_b200 import scene as S
 from onereel_b200.hunyuan15 import _attend, _layout_key
 from onereel_b200.layout import SceneLayout
@@ -72,8 +74,6 @@ class Processor:
     def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, rotary_emb=None):
         """wan.py:81-108"""
         ctx, T, lay = self.ctx, self.ctx.T, self.ctx.layout
-        if ctx.memory:
-            raise NotImplementedError('bounded memory is not on the B200 path')
         a, b = ctx.own[D.rank()]
         if self.kind == 'cross':
             pieces = ([(j, lo, hi) for j, lo, hi in ctx.ring.local[D.rank()] if hi > lo] if ctx.run_mode == 'ring' else
@@ -96,6 +96,8 @@ class Processor:
             qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
             r = ctx.attn_override(self.layer, qa, ka, va)
             o = comm.a2a_tokens(self.ranges(qa, ka, va) if r is None else r)
+        elif ctx.memory:
+            o = self.memory(q, k, v)
         elif ctx.run_mode == 'ulysses' or D.world() == 1:
             o = comm.a2a_tokens(self.ranges(comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)))
         elif ctx.run_mode == 'ring':
@@ -154,6 +156,37 @@ class Processor:
         return ov
 
 
+
+    def memory(self, q, k, v):
+        """wan.py:154-173: bounded cross-scene memory (onereel_b200.memory). One GPU / Ulysses: all tokens of the
+        local heads; K/V gathering: this rank's scene pieces, with the missing scene frames and every boundary
+        candidate received from their owners."""
+        ctx, T, lay = self.ctx, self.ctx.T, self.ctx.layout
+        if ctx._mem is None:
+            ctx._mem = MEM.MemoryAttention(MEM.BoundaryMemory(ctx.memory))
+        ulysses = ctx.run_mode == 'ulysses' or D.world() == 1
+        rk = rv = None
+        if ulysses:
+            q, k, v = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
+            own, remote_index = (0, lay.n_frames * T), []
+            scenes = [(j, (lo * T, hi * T)) for j, (lo, hi) in enumerate(lay.ranges)]
+        else:
+            own = tuple(ctx.own[D.rank()])
+            ex = comm.HaloExchange(lay, ctx.own, T, k, v, extra=MEM.candidate_frames(lay)[0])
+            ex.wait()
+            remote_index, rk, rv = ex.remote_index, ex.remote_k, ex.remote_v
+            scenes = S.pieces(lay, T, own)[0]
+        Hl, Dh = q.shape[1:]
+        pk = ('wan', _layout_key(lay), T, own, tuple(map(tuple, remote_index)), Hl, Dh, str(q.device))
+        plan = ctx._mem.plans.get(pk)
+        if plan is None:
+            plan = ctx._mem.plans[pk] = MEM.MemoryPlan.for_rank(lay, T, None, own, remote_index, scenes, set(),
+                                                                q.device)
+        o = torch.empty_like(q)
+        ctx._mem.run((self.layer, ctx.cond()), plan, q, k, v, None, None, None, o, None, rk, rv)
+        return comm.a2a_tokens(o) if ulysses else o
+
+
 def plan_parallel(ctx: Context, heads: int):
     """wan.py:248-271"""
     n, lay = D.world(), ctx.layout
@@ -167,8 +200,6 @@ def plan_parallel(ctx: Context, heads: int):
         ctx.run_mode, ctx.own = 'ring', ctx.ring.own
         ctx.path = dict(path='ring', V_R=ctx.ring.volume(), V_U=4 * lay.n_frames * ctx.T * (n - 1) / n ** 2)
         return
-    if ctx.memory:
-        raise NotImplementedError('bounded memory is not on the B200 path')
     gather = comm.partition(lay, n, ctx.T, 'scene', None, ctx.memory)
     ctx.path = comm.choose_path(lay, gather, ctx.T, ctx.theta)
     ctx.path['ulysses_ok'] = lay.n_frames * ctx.T % n == 0 and heads % n == 0

@@ -119,6 +119,14 @@ def main():
             mv, mt = HY.Processor(mc, 0).memory(*(x[ma:mb].contiguous() for x in (q, k, v)), eq, ek, ev)
             assert torch.equal(mv, mref_v[ma:mb]), (lengths, r, 'memory gather video')
             assert torch.equal(mt, mref_t), (lengths, r, 'memory gather text')
+            D.world, D.rank = (lambda: 1), (lambda: 0)
+            wm_ref = WN.Processor(WN.Context(lay_m, T=T, own=[(0, L)], memory=8, fwd=1), 'self', None, 0).memory(q, k, v)
+            D.world, D.rank = saved
+            wown = comm.partition(lay_m, n, T, 'scene', None, 8)
+            wa, wb = wown[r]
+            wm = WN.Processor(WN.Context(lay_m, T=T, own=wown, memory=8, fwd=1), 'self', None, 0).memory(
+                *(x[wa:wb].contiguous() for x in (q, k, v)))
+            assert torch.equal(wm, wm_ref[wa:wb]), (lengths, r, 'wan memory gather')
             if L % n == 0 and H % n == 0:
                 uown = comm.partition(lay_m, n, T, 'ulysses')
                 ua, ub = uown[r]

@@ -55,3 +55,57 @@ def test_memory_attention_matches_reference(lengths, M, counts):
         ref_v, ref_t = _reference(q, k, v, eq, ek, ev, lay, T, rows[rep], owner[rep], valid, tr)
         assert rel(ov, ref_v) < 2e-2, (call, rel(ov, ref_v))
         assert rel(ot, ref_t) < 2e-2, (call, rel(ot, ref_t))
+
+
+def test_wan_memory_matches_reference():
+    """Wan self-attention with the bounded memory (no joint text): scene frames plus foreign representatives"""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a B200')
+    from onereel_b200 import attention as A, wan as WN
+    from onereel_b200.layout import SceneLayout
+    torch.manual_seed(3)
+    T, H, Dh, M = 16, 4, 128, 6
+    lay = SceneLayout([4, 3, 5], halo=0)
+    S = lay.n_frames * T
+    ctx = WN.Context(lay, T=T, own=[(0, S)], memory=M, fwd=1)
+    q, k, v = (torch.randn(S, H, Dh, device='cuda', dtype=torch.bfloat16) for _ in range(3))
+    o = WN.Processor(ctx, 'self', None, 0).memory(q, k, v)
+    torch.cuda.synchronize()
+    A.check()
+    rows, owner = MEM.candidates(lay, T, 'cuda')
+    rep, valid = MEM.BoundaryMemory(M).select((0, True), k[rows])
+    empty = torch.zeros(0, H, Dh, device='cuda', dtype=torch.bfloat16)
+    ref, _ = _reference(q, k, v, empty, empty, empty, lay, T, rows[rep], owner[rep], valid, [(0, 0)] * lay.n_scenes)
+    rel = ((o.float() - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, rel
+
+
+def test_reference_style_frame_plan_call():
+    """the reference's own call shape (tests/test_onereel_memory.py:11-17): frame_plan over concatenated video+text
+    buffers, MemoryAttention(BoundaryMemory(M))(key, q, k, v, plan) -> [Sq + text, H, D]"""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a B200')
+    from onereel_b200 import attention as A
+    from onereel_b200.layout import SceneLayout
+    torch.manual_seed(4)
+    lengths, M, counts = [3, 5, 2, 4], 8, [5, 7, 3, 6]
+    T, H, Dh = 16, 4, 64
+    lay = SceneLayout(lengths, halo=0)
+    S = lay.n_frames * T
+    tr, c = [], 0
+    for m in counts:
+        tr.append((c, c + m))
+        c += m
+    q, k, v = (torch.randn(S, H, Dh, device='cuda', dtype=torch.bfloat16) for _ in range(3))
+    eq, ek, ev = (torch.randn(c, H, Dh, device='cuda', dtype=torch.bfloat16) for _ in range(3))
+    plan = MEM.frame_plan(lay, T, torch.arange(S), S, [(j, lo * T, hi * T) for j, (lo, hi) in enumerate(lay.ranges)],
+                          tr, set(range(lay.n_scenes)), S, 'cuda')
+    out = MEM.MemoryAttention(MEM.BoundaryMemory(M))(('l0', True), torch.cat([q, eq]), torch.cat([k, ek]),
+                                                    torch.cat([v, ev]), plan)
+    torch.cuda.synchronize()
+    A.check()
+    rows, owner = MEM.candidates(lay, T, 'cuda')
+    rep, valid = MEM.BoundaryMemory(M).select(('l0', True), k[rows])
+    ref_v, ref_t = _reference(q, k, v, eq, ek, ev, lay, T, rows[rep], owner[rep], valid, tr)
+    rel = lambda a, b: ((a.float() - b).norm() / b.norm()).item()
+    assert rel(out[:S], ref_v) < 2e-2 and rel(out[S:], ref_t) < 2e-2

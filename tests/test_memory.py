@@ -63,7 +63,8 @@ def test_pieces_match_reference_frame_plan():
             else:
                 remote_index = S.remote_index_of(lay, T, own_all, r, lambda l, t, o: comm.needed(l, t, o, cand))
                 scenes, text_for = S.pieces(lay, T, own)
-            plan = MEM.MemoryPlan(lay, T, counts, own, remote_index, scenes, text_for, 2, 64, 8, 'cpu')
+            plan = MEM.MemoryPlan.for_rank(lay, T, counts, own, remote_index, scenes, text_for, 'cpu')
+            plan.compile(2, 64, 8)
             mine, Sq = {}, own[1] - own[0]
             for seg in plan.segs:
                 if seg.lq == 0:                 # the reference drops pieces without queries (memory.py:121)
