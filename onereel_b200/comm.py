@@ -147,12 +147,47 @@ def choose_path(layout, own, T: int, theta: float, extra=()) -> dict:
 
 # ------------------------------------------------------------------------------------------------ K/V gathering
 
+def _intersect(x, y) -> list[tuple[int, int]]:
+    """intersection of two sorted lists of disjoint intervals"""
+    out, i, j = [], 0, 0
+    while i < len(x) and j < len(y):
+        lo, hi = max(x[i][0], y[j][0]), min(x[i][1], y[j][1])
+        if lo < hi:
+            out.append((lo, hi))
+        if x[i][1] < y[j][1]:
+            i += 1
+        else:
+            j += 1
+    return out
+
+
+def _subtract(x, y) -> list[tuple[int, int]]:
+    """x minus y, both sorted lists of disjoint intervals"""
+    out = []
+    for lo, hi in x:
+        cur = lo
+        for u, w in y:
+            if w <= cur or u >= hi:
+                continue
+            if u > cur:
+                out.append((cur, u))
+            cur = max(cur, w)
+        if cur < hi:
+            out.append((cur, hi))
+    return out
+
+
 class HaloExchange:
-    """comm.py:126-201. Posts the K/V exchange of one layer: rank r sends every peer the tokens of its range that the
-    peer reads and receives the tokens it reads from their owners (per peer: K then V of each interval, in order on
-    both sides, as the reference). Received intervals land back to back in one buffer per tensor:
-    `remote_index` = [(token lo, token hi, buffer row of lo)], `remote_k` / `remote_v` = the buffers.
-    heads: exchange only these heads (contiguous copies are made, as the reference does)."""
+    """comm.py:126-201. Posts the K/V exchange of one layer: rank r receives the tokens it reads from their owners and
+    sends every peer the tokens of its range that the peer reads. Received intervals land back to back in one buffer
+    per tensor: `remote_index` = [(token lo, token hi, buffer row of lo)], `remote_k` / `remote_v` = the buffers.
+    heads: exchange only these heads (contiguous copies are made, as the reference does).
+
+    Rows that every other rank reads (frame-memory frames, shared by every scene, are the common case) travel as one
+    NCCL broadcast from their owner instead of one send per peer: on NVSwitch the broadcast leaves the owner once and
+    is replicated by the switch (NVLS) or along a ring, where the reference's per-peer sends leave the owner n - 1
+    times. Everything else moves point to point, per peer K then V of each interval in token order on both sides, as
+    the reference. Every rank derives the same operation list from the global plan, so the collectives match."""
 
     def __init__(self, layout, own, T, k, v, extra=(), heads=None):
         if heads is not None:
@@ -162,30 +197,50 @@ class HaloExchange:
         self.a, self.b = own[r]
         self.works, self.keep, self.remote_index = [], [k, v], []
         self.remote_k = self.remote_v = None
+        self.broadcast_rows = 0                  # rows this rank takes part in broadcasting (sent or received)
         if n == 1:
             return
-        need = [needed(layout, T, o, extra) for o in own]
+        need = [sorted(needed(layout, T, o, extra)) for o in own]
+        # per owner p: the intervals of its range that every other rank reads (broadcast when n > 2)
+        common = []
+        for p in range(n):
+            c = [tuple(own[p])] if n > 2 else []
+            for q in range(n):
+                if q != p and c:
+                    c = _intersect(c, need[q])
+            common.append(c)
         recv = [(p, lo, hi) for p in range(n) if p != r for lo, hi in clip(need[r], *own[p])]
         rows = sum(hi - lo for _, lo, hi in recv)
         self.remote_k = k.new_empty((rows,) + tuple(k.shape[1:]))
         self.remote_v = v.new_empty((rows,) + tuple(v.shape[1:]))
-        ops, off, recv_ops = [], 0, {}
+        off = 0
         for p, lo, hi in sorted(recv, key=lambda x: x[1]):
             self.remote_index.append((lo, hi, off))
-            recv_ops.setdefault(p, []).append((self.remote_k[off:off + hi - lo], self.remote_v[off:off + hi - lo]))
             off += hi - lo
+
+        def recv_rows(lo, hi):
+            x, y, o = next(t for t in self.remote_index if t[0] <= lo and hi <= t[1])
+            return self.remote_k[o + lo - x:o + hi - x], self.remote_v[o + lo - x:o + hi - x]
         g = D.group()
+        for p in range(n):
+            for lo, hi in common[p]:
+                bk, bv = ((k[lo - self.a:hi - self.a], v[lo - self.a:hi - self.a]) if p == r else recv_rows(lo, hi))
+                for x in (bk, bv):
+                    self.works.append(dist.broadcast(x, D.peer_rank(p), group=g, async_op=True))
+                self.broadcast_rows += hi - lo
+        ops = []
         for p in range(n):
             if p == r:
                 continue
-            for lo, hi in clip(need[p], self.a, self.b):
+            for lo, hi in _subtract(clip(need[p], self.a, self.b), common[r]):
                 for x in (k, v):
                     ops.append(dist.P2POp(dist.isend, x[lo - self.a:hi - self.a], D.peer_rank(p), group=g))
-            for bk, bv in recv_ops.get(p, []):
+            for lo, hi in _subtract(clip(need[r], *own[p]), common[p]):
+                bk, bv = recv_rows(lo, hi)
                 ops += [dist.P2POp(dist.irecv, bk, D.peer_rank(p), group=g),
                         dist.P2POp(dist.irecv, bv, D.peer_rank(p), group=g)]
         if ops:
-            self.works = dist.batch_isend_irecv(ops)
+            self.works += dist.batch_isend_irecv(ops)
 
     def wait(self):
         for w in self.works:

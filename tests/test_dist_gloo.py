@@ -1,5 +1,5 @@
 """The collectives of the parallel paths on CPU gloo ranks (world size 2 and 3): the K/V exchange lands exactly the
-rows each rank's compiled plan expects, the text-row P2P and the Ulysses all-to-all round trip move the right rows,
+rows each rank's compiled plan expects (at world 3 rows every peer reads arrive by broadcast), the text-row P2P and the Ulysses all-to-all round trip move the right rows,
 gather_tokens reassembles unequal ranges — the reference's tests/dist_onereel_gather.py checks, without a GPU."""
 import os
 import socket
@@ -26,6 +26,7 @@ def _worker(rank, world, port, q):
         D.init('gloo', timeout_s=60)
         r, n = D.rank(), D.world()
         T, H, Dh = 16, 2, 8
+        bcast = 0
         for lengths, halo, extra in (([3, 5, 2, 4, 6], 0, True), ([10, 1, 1, 2], 2, False), ([5, 2, 7], 1, True)):
             g = torch.Generator().manual_seed(len(lengths))
             lay = SceneLayout(lengths, halo=halo)
@@ -38,6 +39,7 @@ def _worker(rank, world, port, q):
             a, b = own[r]
             ex = comm.HaloExchange(lay, own, T, k[a:b].contiguous(), v[a:b].contiguous())
             ex.wait()
+            bcast += ex.broadcast_rows
             assert ex.remote_index == S.remote_index_of(lay, T, own, r, comm.needed)
             for lo, hi, off in ex.remote_index:                    # every received row is the sender's row
                 assert torch.equal(ex.remote_k[off:off + hi - lo], k[lo:hi])
@@ -62,6 +64,8 @@ def _worker(rank, world, port, q):
             # gather_tokens over the unequal ranges
             full = torch.arange(L, dtype=torch.float32)[None, :, None].expand(1, L, 3).contiguous()
             assert torch.equal(comm.gather_tokens(full[:, a:b].contiguous(), own), full)
+        # at world 3 the frame every scene reads (extra frame F - 1) travels as a broadcast from its owner
+        assert n < 3 or bcast > 0, 'no broadcast exercised'
         # Ulysses all-to-all round trip on an equal split
         S_, H4 = 6 * n, 2 * n
         x = torch.randn(S_, H4, Dh, generator=torch.Generator().manual_seed(5))
