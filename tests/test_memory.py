@@ -108,3 +108,24 @@ def test_representative_is_nearest_member():
             members = (z == z[r]).nonzero().flatten()
             d = (xn[h, members] - c[h, z[r]]).pow(2).sum(-1)
             assert d.min() >= (xn[h, r] - c[h, z[r]]).pow(2).sum() - 1e-6
+
+
+def test_frame_plan_matches_reference_at_world_1():
+    """the reference-style frame_plan (memory.py:126-140) on one rank: same pieces, keys and candidates"""
+    cases = [c for c in json.loads((G / 'memory.json').read_text())['plans'] if c['n'] == 1]
+    assert cases
+    for c in cases:
+        lay = SceneLayout(c['lengths'], halo=0)
+        T, counts = c['T'], c['counts']
+        L_ = lay.n_frames * T
+        tr = S.text_ranges(counts)
+        plan = MEM.frame_plan(lay, T, torch.arange(L_), L_, [(j, lo * T, hi * T) for j, (lo, hi) in
+                                                           enumerate(lay.ranges)], tr, set(range(lay.n_scenes)), L_,
+                              'cpu')
+        mine = {}
+        for seg in plan.segs:
+            keys = [row if row < L_ else -(row - L_ + 1) for _, lo, hi in seg.kv for row in range(lo, hi)]
+            mine[(seg.kind == 'v', seg.scene)] = ([seg.q[1], seg.q[2]], keys)
+        ref = {(p['mem'], p['scene']): (p['q'], p['keys']) for p in c['ranks'][0]['pieces']}
+        assert mine == ref, c['lengths']
+        assert plan.cand_local_rows.tolist() == c['ranks'][0]['cand']
