@@ -38,6 +38,8 @@ extern "C" {
 #define ORL_ERR_TENSOR_MAP (-5)   /* the driver rejected a tensor map */
 #define ORL_ERR_LAUNCH (-6)       /* kernel launch failed */
 #define ORL_ERR_CAPACITY (-7)     /* a caller buffer is too small */
+#define ORL_ERR_COMM (-8)         /* NCCL reported an error (the communicator is aborted after a failed wait) */
+#define ORL_ERR_TIMEOUT (-9)      /* orl_comm_wait gave up: the communicator was aborted */
 
 /* One attention work item: up to 256 query rows of one segment and one head. */
 typedef struct orl_attn_work {
@@ -200,6 +202,52 @@ ORL_API int orl_needed(const orl_layout* layout, long long T, long long own_lo, 
 /* Eq. 2 path choice for a partition (comm.py:99-112). */
 ORL_API int orl_choose_path(const orl_layout* layout, long long T, const int64_t* bounds, int n, double theta,
                             const int32_t* extra, int n_extra, orl_path* path);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Collectives of the multi-GPU path over NCCL (loaded with dlopen at the first call; a process that already loaded
+ * NCCL shares it). They replace the torch.distributed calls of src/onereel/parallel/comm.py for C / C++ callers:
+ * HaloExchange (126-201, batch_isend_irecv of K then V per interval and peer) -> orl_comm_exchange; rows every peer
+ * reads -> orl_comm_broadcast; a2a_heads / a2a_tokens (276-295, all_to_all_single) -> orl_comm_all_to_all; the text
+ * rows' dist.all_reduce -> orl_comm_all_reduce_f32. Operations are enqueued on the caller's stream; orl_comm_wait is
+ * the timeout-aware completion check. */
+typedef struct orl_comm orl_comm;  /* opaque: one NCCL communicator of one rank */
+
+typedef struct orl_p2p {
+  int32_t peer;    /* rank of the other side */
+  int32_t pad;
+  void* ptr;       /* device buffer */
+  long long bytes;
+} orl_p2p;
+
+/* 1 if NCCL could be loaded, else 0. */
+ORL_API int orl_comm_available(void);
+
+/* A new NCCL unique id (128 bytes) on the rank that creates the communicator; the caller distributes it. */
+ORL_API int orl_comm_unique_id(uint8_t* id_out);
+
+/* Joins the communicator of `world` ranks identified by `id` as `rank`, on CUDA device `device` (blocks until every
+ * rank has joined). */
+ORL_API int orl_comm_init(orl_comm** comm, const uint8_t* id, int world, int rank, int device);
+
+ORL_API int orl_comm_destroy(orl_comm* comm);
+
+/* One grouped exchange: every send and receive of the lists, per peer in list order on both sides. */
+ORL_API int orl_comm_exchange(orl_comm* comm, const orl_p2p* sends, int n_send, const orl_p2p* recvs, int n_recv,
+                              void* stream);
+
+/* In-place broadcast of `bytes` from `root`. */
+ORL_API int orl_comm_broadcast(orl_comm* comm, void* buf, long long bytes, int root, void* stream);
+
+/* Equal-split all-to-all: block p (bytes_per_peer) of send goes to rank p, block p of recv comes from rank p. */
+ORL_API int orl_comm_all_to_all(orl_comm* comm, const void* send, void* recv, long long bytes_per_peer, void* stream);
+
+/* In-place sum over the ranks of n floats. */
+ORL_API int orl_comm_all_reduce_f32(orl_comm* comm, float* buf, long long n, void* stream);
+
+/* Waits until `stream` is idle, polling NCCL's asynchronous error. An NCCL error or `timeout_ns` without completion
+ * aborts the communicator (its in-flight operations end) and returns ORL_ERR_COMM / ORL_ERR_TIMEOUT; the
+ * communicator is then unusable except for orl_comm_destroy. */
+ORL_API int orl_comm_wait(orl_comm* comm, void* stream, unsigned long long timeout_ns);
 
 #ifdef __cplusplus
 }

@@ -34,6 +34,11 @@ class Layout(ctypes.Structure):
                 ('extra_offsets', P_I32), ('extra_frames', P_I32)]
 
 
+class P2P(ctypes.Structure):
+    """orl_p2p: one send or receive of orl_comm_exchange"""
+    _fields_ = [('peer', ctypes.c_int32), ('pad', ctypes.c_int32), ('ptr', ctypes.c_void_p), ('bytes', ctypes.c_longlong)]
+
+
 class Path(ctypes.Structure):
     """orl_path"""
     _fields_ = [('remote_rows', ctypes.c_longlong), ('V_G', ctypes.c_double), ('V_U', ctypes.c_double),
@@ -71,6 +76,15 @@ SIGNATURES = {
     'orl_partition': (c_int, [c_vp, c_ll, c_int, c_int, P_I32, c_ll, c_int, P_I64]),
     'orl_needed': (c_int, [c_vp, c_ll, c_ll, c_ll, P_I32, c_int, P_I64, c_int]),
     'orl_choose_path': (c_int, [c_vp, c_ll, P_I64, c_int, ctypes.c_double, P_I32, c_int, c_vp]),
+    'orl_comm_available': (c_int, []),
+    'orl_comm_unique_id': (c_int, [c_vp]),
+    'orl_comm_init': (c_int, [ctypes.POINTER(c_vp), c_vp, c_int, c_int, c_int]),
+    'orl_comm_destroy': (c_int, [c_vp]),
+    'orl_comm_exchange': (c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp]),
+    'orl_comm_broadcast': (c_int, [c_vp, c_vp, c_ll, c_int, c_vp]),
+    'orl_comm_all_to_all': (c_int, [c_vp, c_vp, c_vp, c_ll, c_vp]),
+    'orl_comm_all_reduce_f32': (c_int, [c_vp, c_vp, c_ll, c_vp]),
+    'orl_comm_wait': (c_int, [c_vp, c_vp, ctypes.c_ulonglong]),
 }
 
 _lib = None

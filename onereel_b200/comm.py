@@ -187,9 +187,10 @@ class HaloExchange:
     NCCL broadcast from their owner instead of one send per peer: on NVSwitch the broadcast leaves the owner once and
     is replicated by the switch (NVLS) or along a ring, where the reference's per-peer sends leave the owner n - 1
     times. Everything else moves point to point, per peer K then V of each interval in token order on both sides, as
-    the reference. Every rank derives the same operation list from the global plan, so the collectives match."""
+    the reference. Every rank derives the same operation list from the global plan, so the collectives match.
+    collectives: None (torch.distributed) or an onereel_b200.collectives.NcclComm (the C ABI's orl_comm_*)."""
 
-    def __init__(self, layout, own, T, k, v, extra=(), heads=None):
+    def __init__(self, layout, own, T, k, v, extra=(), heads=None, collectives=None):
         if heads is not None:
             k, v = k[:, heads].contiguous(), v[:, heads].contiguous()
         self.T, self.k, self.v, self.L = T, k, v, layout.n_frames * T
@@ -222,27 +223,45 @@ class HaloExchange:
             x, y, o = next(t for t in self.remote_index if t[0] <= lo and hi <= t[1])
             return self.remote_k[o + lo - x:o + hi - x], self.remote_v[o + lo - x:o + hi - x]
         g = D.group()
+        self.collectives = collectives
+        bcasts, sends, recvs = [], [], []
         for p in range(n):
             for lo, hi in common[p]:
                 bk, bv = ((k[lo - self.a:hi - self.a], v[lo - self.a:hi - self.a]) if p == r else recv_rows(lo, hi))
-                for x in (bk, bv):
-                    self.works.append(dist.broadcast(x, D.peer_rank(p), group=g, async_op=True))
+                bcasts += [(bk, p), (bv, p)]
                 self.broadcast_rows += hi - lo
-        ops = []
         for p in range(n):
             if p == r:
                 continue
             for lo, hi in _subtract(clip(need[p], self.a, self.b), common[r]):
-                for x in (k, v):
-                    ops.append(dist.P2POp(dist.isend, x[lo - self.a:hi - self.a], D.peer_rank(p), group=g))
+                sends += [(p, k[lo - self.a:hi - self.a]), (p, v[lo - self.a:hi - self.a])]
             for lo, hi in _subtract(clip(need[r], *own[p]), common[p]):
                 bk, bv = recv_rows(lo, hi)
-                ops += [dist.P2POp(dist.irecv, bk, D.peer_rank(p), group=g),
-                        dist.P2POp(dist.irecv, bv, D.peer_rank(p), group=g)]
+                recvs += [(p, bk), (p, bv)]
+        if collectives is not None:
+            for x, p in bcasts:
+                collectives.broadcast(x, D.peer_rank(p))
+            if sends or recvs:
+                collectives.exchange([(D.peer_rank(p), x) for p, x in sends], [(D.peer_rank(p), x) for p, x in recvs])
+            return
+        for x, p in bcasts:
+            self.works.append(dist.broadcast(x, D.peer_rank(p), group=g, async_op=True))
+        # per peer: sends (K then V of each interval in token order), then receives, as batch_isend_irecv expects
+        ops = []
+        for p in range(n):
+            if p == r:
+                continue
+            ops += [dist.P2POp(dist.isend, x, D.peer_rank(p), group=g) for q, x in sends if q == p]
+            ops += [dist.P2POp(dist.irecv, x, D.peer_rank(p), group=g) for q, x in recvs if q == p]
         if ops:
             self.works += dist.batch_isend_irecv(ops)
 
-    def wait(self):
+    def wait(self, timeout_s: float | None = None):
+        """the exchange's results are usable on the current stream after this (torch.distributed: Work.wait;
+        NcclComm: a device-side dependency, or the timeout-aware host wait when timeout_s is given)"""
+        if getattr(self, 'collectives', None) is not None:
+            self.collectives.wait(timeout_s)
+            self.collectives = None
         for w in self.works:
             w.wait()
         self.works = []

@@ -17,6 +17,8 @@ extern "C" const char* orl_error_string(int code) {
     case ORL_ERR_TENSOR_MAP: return "the driver rejected a TMA tensor map";
     case ORL_ERR_LAUNCH: return "kernel launch failed";
     case ORL_ERR_CAPACITY: return "caller buffer too small";
+    case ORL_ERR_COMM: return "NCCL error (communicator aborted after a failed wait)";
+    case ORL_ERR_TIMEOUT: return "collective wait timed out (communicator aborted)";
     default: return "unknown error";
   }
 }

@@ -44,7 +44,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         objs.append(str(obj))
     tmp = LIB.with_suffix('.so.tmp')
     subprocess.run([NVCC, '-shared', '-gencode', 'arch=compute_100a,code=sm_100a', *objs, '-o', str(tmp),
-                    '-lcudart'], check=True)
+                    '-lcudart', '-ldl'], check=True)
     os.replace(tmp, LIB)
     return LIB
 

@@ -107,3 +107,21 @@ def test_layout_api_matches_golden():
             assert list(lay.key_range(j)) == c['key_range'][j]
     for e in data['even']:
         assert SceneLayout.even(e['n_frames'], e['n_scenes']).lengths == e['lengths']
+
+
+def test_comm_abi_rejects_bad_arguments_without_a_gpu():
+    """the NCCL wrappers validate their arguments before touching NCCL or CUDA"""
+    import ctypes
+    from onereel_b200 import _lib as L
+    lib = L.lib()
+    assert lib.orl_comm_exchange(None, None, 0, None, 0, None) == -1
+    assert lib.orl_comm_broadcast(None, None, 0, 0, None) == -1
+    assert lib.orl_comm_all_to_all(None, None, None, 0, None) == -1
+    assert lib.orl_comm_all_reduce_f32(None, None, 0, None) == -1
+    assert lib.orl_comm_wait(None, None, 0) == -1
+    assert lib.orl_comm_destroy(None) == -1
+    h = ctypes.c_void_p()
+    assert lib.orl_comm_init(ctypes.byref(h), None, 2, 0, 0) == -1          # no id
+    assert lib.orl_comm_unique_id(None) == -1
+    assert lib.orl_error_string(-8) == b'NCCL error (communicator aborted after a failed wait)'
+    assert lib.orl_error_string(-9) == b'collective wait timed out (communicator aborted)'

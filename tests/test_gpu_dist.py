@@ -33,3 +33,16 @@ def test_parallel_paths_match_single_gpu(n):
     p = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stdout[-4000:] + p.stderr[-4000:]
     assert p.stdout.count('PASS') == 5, p.stdout
+
+
+@pytest.mark.parametrize('n', [2])
+def test_c_abi_collectives_match_torch_distributed(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f'needs {n} GPUs')
+    env = dict(os.environ, NCCL_NVLS_ENABLE='0', PYTHONPATH=str(ROOT))
+    cmd = ['timeout', '-k', '30', '300', sys.executable, '-m', 'torch.distributed.run', '--nnodes=1',
+           f'--nproc-per-node={n}', '--master-addr', '127.0.0.1', '--master-port', str(_free_port()),
+           str(ROOT / 'tests' / 'dist_comm_worker.py')]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert p.returncode == 0, p.stdout[-4000:] + p.stderr[-4000:]
+    assert 'PASS' in p.stdout, p.stdout
