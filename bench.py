@@ -39,7 +39,7 @@ CFG5 = dict(scene_frames=31, T=880, text=0, heads=24, dim=128)
 CFG4 = dict(lengths=[31, 31, 31, 31], T=1590, text=128, heads=16, dim=128, memory=[0, 31, 62, 93], hidden=2048,
             blocks=54, frame_hw=(30, 53))
 METRIC = 'scene-packed attn TFLOP/s/GPU; DiT step latency @1/2/4/8 B200'
-# DRAM bytes / algorithmic bytes of the attention kernel, from the small-case ncu capture (profiles/attn_fwd_cfg2.md)
+# DRAM bytes / algorithmic bytes of the attention kernel, from the small-case ncu capture summarised in profiles/
 TRAFFIC_PER_ALG_BYTE = 373.86 / 392.9
 
 
@@ -380,7 +380,7 @@ def run_layer(args, last=True):
                                        else None),
                               traffic_note='bytes per step of the attention launches: their algorithmic bytes (Q + O '
                                            '+ K/V once per segment) x the DRAM/algorithmic ratio of the small-case '
-                                           'ncu capture (profiles/attn_fwd_cfg2.md)',
+                                           'ncu capture (summarised in profiles/)',
                               frac_of_sustained=achieved / peak_sus if peak_sus else None,
                               kernel='attn_fwd_kernel<128> (all attention launches of a step, rank 0)',
                               peak_source=f'{peak_kind} bf16 burst'),

@@ -1,6 +1,6 @@
 """The reference's CPU path of the scene-packed attention layer — TEST / BASELINE INFRASTRUCTURE ONLY.
 
-BASELINE.md's CPU baseline is the reference's own scene processor (src/onereel/models/hunyuan15.py:212-251 with
+The CPU baseline is the reference's own scene processor (src/onereel/models/hunyuan15.py:212-251 with
 `_segments` 153-170 and attention.packed 65-71) with the FlashAttention varlen call replaced by per-segment fp32
 `torch.nn.functional.scaled_dot_product_attention` on the host cores. This module restates that path on the CPU:
 gather each segment's rows (the reference's torch.cat), one fp32 SDPA per segment, scatter the outputs. It is what

@@ -1,6 +1,6 @@
 """Generate the golden fixtures of tests/golden/ by running the OneReel reference's own Python code on the CPU.
 
-Run in a container that has the reference checked out (default path below, or ONEREEL_REF=<repo root>):
+Run where the reference is checked out (next to this repository by default, or ONEREEL_REF=<repo root>):
     python tests/golden/make_golden.py
 Writes layout.json, planner.json, segments.json and cfg1.npz next to this file. The fixtures pin both the CPU oracle
 (oracle/) and the product's native planner / pack plan; the GPU box never needs the reference.
@@ -34,7 +34,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get('ONEREEL_REF', '/root/reference'))
+REF = Path(os.environ.get('ONEREEL_REF', Path(__file__).resolve().parents[3] / 'reference'))
 sys.path.insert(0, str(REF / 'src'))
 HERE = Path(__file__).resolve().parent
 
