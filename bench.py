@@ -408,7 +408,9 @@ def run_dit_step(args):
     lay = cfg_layout(cfg)
     T, H, Dh, C = cfg['T'], cfg['heads'], cfg['dim'], cfg['hidden']
     counts = [cfg['text']] * lay.n_scenes
-    ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts})
+    if args.overlap == 'auto':                   # measured on 4 B200: the LSE split does not pay for the DiT step
+        args.overlap = 'none'
+    ctx = HY.Context(lay, mode=args.mode, T=T, counts={True: counts, False: counts}, overlap=args.overlap)
     HY.plan_parallel(ctx, H)
     a, b = ctx.own[rank]
     model = standin.build(ctx, dev, C, H, cfg['blocks'])
@@ -451,7 +453,7 @@ def run_dit_step(args):
                               dtype='bf16', data='synthetic (random-init stand-in, seeded)',
                               config=dict(workload='cfg4: one denoising step (2 CFG forwards x 54 blocks) of the '
                                                    'HunyuanVideo-1.5-architecture stand-in', layout=cfg,
-                                          run_mode=ctx.run_mode, path=ctx.path, own=ctx.own,
+                                          run_mode=ctx.run_mode, path=ctx.path, own=ctx.own, overlap=ctx.overlap,
                                           flop_per_step=dict(gemm=gemm, attention=attn)),
                               achieved_tflops=(gemm + attn) / (ms * 1e-3) / 1e12, clocks=clk.summary())), flush=True)
     D.shutdown()
