@@ -177,6 +177,24 @@ def _subtract(x, y) -> list[tuple[int, int]]:
     return out
 
 
+def exchange_plan(layout, own, T: int, extra=()):
+    """the operation lists of one K/V exchange, for every rank at once (every rank computes the same lists):
+    need[r] = the token intervals rank r reads outside its range; common[p] = the intervals of owner p's range that
+    every other rank reads (broadcast from p, when there are more than 2 ranks); p2p[(p, q)] = the remaining
+    intervals owner p sends to reader q, in token order"""
+    n = len(own)
+    need = [sorted(needed(layout, T, o, extra)) for o in own]
+    common = []
+    for p in range(n):
+        c = [tuple(own[p])] if n > 2 else []
+        for q in range(n):
+            if q != p and c:
+                c = _intersect(c, need[q])
+        common.append(c)
+    p2p = {(p, q): _subtract(clip(need[q], *own[p]), common[p]) for p in range(n) for q in range(n) if p != q}
+    return need, common, p2p
+
+
 class HaloExchange:
     """comm.py:126-201. Posts the K/V exchange of one layer: rank r receives the tokens it reads from their owners and
     sends every peer the tokens of its range that the peer reads. Received intervals land back to back in one buffer
@@ -201,15 +219,7 @@ class HaloExchange:
         self.broadcast_rows = 0                  # rows this rank takes part in broadcasting (sent or received)
         if n == 1:
             return
-        need = [sorted(needed(layout, T, o, extra)) for o in own]
-        # per owner p: the intervals of its range that every other rank reads (broadcast when n > 2)
-        common = []
-        for p in range(n):
-            c = [tuple(own[p])] if n > 2 else []
-            for q in range(n):
-                if q != p and c:
-                    c = _intersect(c, need[q])
-            common.append(c)
+        need, common, p2p = exchange_plan(layout, own, T, extra)
         recv = [(p, lo, hi) for p in range(n) if p != r for lo, hi in clip(need[r], *own[p])]
         rows = sum(hi - lo for _, lo, hi in recv)
         self.remote_k = k.new_empty((rows,) + tuple(k.shape[1:]))
@@ -233,9 +243,9 @@ class HaloExchange:
         for p in range(n):
             if p == r:
                 continue
-            for lo, hi in _subtract(clip(need[p], self.a, self.b), common[r]):
+            for lo, hi in p2p[(r, p)]:
                 sends += [(p, k[lo - self.a:hi - self.a]), (p, v[lo - self.a:hi - self.a])]
-            for lo, hi in _subtract(clip(need[r], *own[p]), common[p]):
+            for lo, hi in p2p[(p, r)]:
                 bk, bv = recv_rows(lo, hi)
                 recvs += [(p, bk), (p, bv)]
         if collectives is not None:

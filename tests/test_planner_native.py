@@ -156,3 +156,39 @@ def test_ring_plan_matches_reference():
         for src in range(c['n']):
             got = {str(j): (None if x is None else x.tolist()) for j, x in plan.keys(src, 'tag').items()}
             assert got == c['keys'][str(src)]
+
+
+def test_exchange_plan_covers_every_read_once():
+    """the K/V exchange's operation lists (broadcast of rows every other rank reads, point to point for the rest) on
+    random layouts for 2..8 ranks: every rank receives exactly the tokens it reads outside its range, each once, and
+    both sides of every point-to-point pair list the same intervals"""
+    import random
+    from onereel_b200 import comm
+    from onereel_b200.layout import SceneLayout
+    rng = random.Random(3)
+    for case in range(120):
+        lengths = [rng.randint(1, 9) for _ in range(rng.randint(1, 9))]
+        lay = SceneLayout(lengths, halo=rng.choice([0, 1, 2]), sides=rng.choice(['adj', 'prev', 'next']))
+        F = lay.n_frames
+        if rng.random() < 0.7:
+            shared = rng.sample(range(F), min(F, rng.randint(1, 3)))        # frame-memory-like: read by every scene
+            lay.extra = {j: sorted(shared) for j in range(lay.n_scenes)}
+        T = rng.choice([2, 4, 7])
+        n = rng.randint(2, 8)
+        if F * T < 2 * n:
+            continue
+        own = comm.partition(lay, n, T, 'scene', [rng.randint(0, 4) for _ in lengths])
+        extra = sorted({f for v in lay.extra.values() for f in v}) if rng.random() < 0.3 else ()
+        need, common, p2p = comm.exchange_plan(lay, own, T, extra)
+        for r in range(n):
+            got = []
+            for p in range(n):
+                if p != r:
+                    got += [iv for iv in common[p]] + p2p[(p, r)]
+            toks = sorted(t for lo, hi in got for t in range(lo, hi))
+            want = sorted(t for lo, hi in need[r] for t in range(lo, hi))
+            assert toks == want, (case, lengths, n, r)
+            for p in range(n):                       # what p broadcasts lies in its own range
+                assert all(own[p][0] <= lo and hi <= own[p][1] for lo, hi in common[p])
+        if n == 2:
+            assert all(not c for c in common)
