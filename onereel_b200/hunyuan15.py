@@ -128,6 +128,36 @@ def shared_positions(ctx, j: int) -> list[int]:
     return [pos[f] for f in shared]
 
 
+def _shift_rows(ctx, j: int):
+    """per shared frame of scene j (shared_frames order), the rotary-table rows a, a + d of two frames d apart in the
+    same spatial order, d = its adjacent position minus its own (hunyuan15.py:136-144): R(a + d) R(a)^-1 moves a key
+    rotated at its own frame to the adjacent one (the temporal angles compose, the spatial ones cancel)"""
+    T = ctx.T
+    a_rows, b_rows = [], []
+    for f, dst in zip(ctx.layout.shared_frames(j), shared_positions(ctx, j)):
+        d = dst - frame_position(ctx, f)
+        a = 0 if d >= 0 else -d
+        a_rows.append(torch.arange(a * T, (a + 1) * T))
+        b_rows.append(torch.arange((a + d) * T, (a + d + 1) * T))
+    return torch.cat(a_rows), torch.cat(b_rows)
+
+
+def _move_shared(ctx, j: int, k: torch.Tensor) -> torch.Tensor:
+    """hunyuan15.py:127-150 with the reference's arguments: k = scene j's keys (own frames, then shared frames) rotated
+    at their own frame index -> the shared frames' keys re-rotated to their adjacent positions, as one rotation by the
+    composed angle (cos(b - a), sin(b - a) from the table rows a, b). Torch ops, for callers holding one scene's keys;
+    the processors do the same inside the packed K with the orl_rope_rows kernel."""
+    lay, T = ctx.layout, ctx.T
+    if not lay.shared_frames(j):
+        return k
+    n = len(lay.frames[j]) * T
+    ar, br = _shift_rows(ctx, j)
+    cos, sin = ctx._rot_full
+    ca, sa, cb, sb = (t.float().to(k.device) for t in (cos[ar], sin[ar], cos[br], sin[br]))
+    x = apply_rotary_emb(k[None, n:], (cb * ca + sb * sa, sb * ca - cb * sa))[0]
+    return torch.cat([k[:n], x.to(k.dtype)])
+
+
 def scene_rope_rows(ctx, device):
     """hunyuan15.py:443-454: per video token row, the rotary row of the same spatial position at its frame index
     within its scene (+ 1 after scene 0)"""
