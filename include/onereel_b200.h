@@ -91,12 +91,14 @@ ORL_API int orl_attn_fwd(const void* q, const void* k, const void* v, void* out,
  * framework's memory pool or allocator hook, or a plugin host that owns all device memory) and so cannot supply the
  * work list and error word orl_attn_fwd needs. Has no counterpart in the reference. The scratch lives in a
  * file-scope device array of the library (about 512 KiB per GPU that loads it, held until the process exits); the
- * call plans on the host (cu_q_host / cu_k_host: HOST int32 [n_seg + 1]) and allocates nothing. Limits: at most 4096
- * segments and 16384 work items (heads x ceil(q rows / 256) summed over segments): larger calls return
- * ORL_ERR_CAPACITY. Calls share the array (it keeps the last call's contents; the error word is cleared per call):
- * calls that overlap on one GPU race, so serialise them per device. The first call on a device looks up the array's
- * address; make it before any stream capture. status_host (optional): when not NULL the call waits for the kernel
- * and stores its timeout bits (0 = ok). */
+ * call orders the segments on the host (cu_q_host / cu_k_host: HOST int32 [n_seg + 1]), passes that table to the
+ * GPU as a kernel parameter and allocates nothing. Limits: at most 1024 segments and 16384 work items (heads x
+ * ceil(q rows / 256) summed over segments): larger calls return ORL_ERR_CAPACITY before any work. q, k, v, out, lse
+ * and the stream must belong to the current device (else ORL_ERR_ARG). Calls share the array (it keeps the last
+ * call's contents; the error word is cleared per call): calls that overlap on one GPU race, so serialise them per
+ * device. The first call on a device looks up the array's address and caches it (a cudaDeviceReset invalidates the
+ * cache); make that first call before any stream capture. status_host (optional): when not NULL the call waits for
+ * the kernel and stores its timeout bits (0 = ok). */
 ORL_API int orl_attn_fwd_noalloc(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
                                  long long nk, int heads, int head_dim, float scale, const int32_t* cu_q_host,
                                  const int32_t* cu_k_host, int n_seg, int* status_host, void* stream);

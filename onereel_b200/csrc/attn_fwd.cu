@@ -292,11 +292,15 @@ __device__ __forceinline__ void softmax_role(const AttnShared& sh, uint32_t tmem
       } else {
         exp_half(0, -mr[0] * scale_log2, -mr[1] * scale_log2, pa, sa0, sa1);   // speculative
         const float mx0 = tile_max(0), mx1 = tile_max(1);
-        const bool redo = (mx0 - mr[0]) * scale_log2 > kMaxJump || (mx1 - mr[1]) * scale_log2 > kMaxJump;
-        if (__any_sync(0xffffffffu, redo)) {
-          m_use0 = fmaxf(mr[0], mx0);
-          m_use1 = fmaxf(mr[1], mx1);
-          const float al0 = ex2((mr[0] - m_use0) * scale_log2), al1 = ex2((mr[1] - m_use1) * scale_log2);
+        const bool redo0 = (mx0 - mr[0]) * scale_log2 > kMaxJump, redo1 = (mx1 - mr[1]) * scale_log2 > kMaxJump;
+        if (__any_sync(0xffffffffu, redo0 || redo1)) {
+          // the warp redoes its tile together (TMEM loads and stores are warp-wide), but only rows whose max jumped
+          // take the new max: the others keep theirs (factor exactly 1, P unchanged), so a row's result never
+          // depends on which rows share its warp or work item
+          m_use0 = redo0 ? fmaxf(mr[0], mx0) : mr[0];
+          m_use1 = redo1 ? fmaxf(mr[1], mx1) : mr[1];
+          const float al0 = redo0 ? ex2((mr[0] - m_use0) * scale_log2) : 1.0f;
+          const float al1 = redo1 ? ex2((mr[1] - m_use1) * scale_log2) : 1.0f;
           exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
           lr[0] *= al0;
           lr[1] *= al1;
@@ -591,25 +595,103 @@ extern "C" int orl_attn_fwd(const void* q, const void* k, const void* v, void* o
 // array below instead: every GPU that loads the library holds it (kNoAllocScratchBytes, about 512 KiB) until the
 // process exits. Its limits: at most kNoAllocMaxSegments segments and kNoAllocMaxItems work items (one item = one
 // head x up to 256 query rows of one segment); larger calls are rejected with ORL_ERR_CAPACITY before any work.
-// Every call shares the array and it keeps the last call's contents: the error word is cleared at the start of each
-// call. Calls whose kernels overlap on one GPU (issued on two streams, or from two host threads) race on the array,
-// so callers serialise their calls per device; calls on different GPUs do not interact (each GPU has its own copy).
-// The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device current)
-// and caches it; make that first call before any stream capture.
+//
+// The host orders the segments (the schedule of orl_attn_plan) into a table that travels as a kernel parameter;
+// a one-block kernel expands it into the work list inside the array and clears the error word, then the attention
+// kernel runs on it. No host buffer is read after the call returns. Every call shares the array and it keeps the
+// last call's contents; calls whose kernels overlap on one GPU (issued on two streams, or from two host threads)
+// race on it, so callers serialise their calls per device; calls on different GPUs do not interact (each GPU has
+// its own copy). The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that
+// device current) and caches it per device ordinal; make that first call before any stream capture. The cached
+// address does not survive cudaDeviceReset (the module, and with it the array, is loaded anew).
 namespace orl {
 
 constexpr int kNoAllocMaxItems = 16384;
-constexpr int kNoAllocMaxSegments = 4096;
+constexpr int kNoAllocMaxSegments = 1024;
 constexpr int kNoAllocHeaderBytes = 256;   // error word at offset 0, work items from offset 256
 constexpr int kNoAllocScratchBytes = kNoAllocHeaderBytes + kNoAllocMaxItems * static_cast<int>(sizeof(AttnWork));
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// the ordered segment table, passed by value as the expand kernel's parameter (about 20 KiB, inside the 32 KiB
+// kernel-parameter limit of sm_70 and later)
+struct NoAllocTable {
+  int n_seg;                          // segments with query rows, in schedule order
+  int heads;
+  int n_items;
+  int pad;
+  int4 seg[kNoAllocMaxSegments];      // (q_row0, q_len, k_row0, k_len)
+  int index[kNoAllocMaxSegments];     // the segment's position in the caller's cu_seqlens
+};
+static_assert(sizeof(NoAllocTable) < 32000, "kernel parameter limit");
+
+// One block: item counts per segment, an inclusive scan in shared memory, then every item written by one thread
+// (item i -> its segment by binary search over the scan). Items of one segment: head-major, 256-row chunks inside.
+__global__ void __launch_bounds__(1024) noalloc_expand_kernel(const __grid_constant__ NoAllocTable tab,
+                                                              AttnWork* __restrict__ work, int* __restrict__ err) {
+  __shared__ int end[kNoAllocMaxSegments];
+  const int t = threadIdx.x;
+  if (t == 0) *err = 0;
+  int cnt = 0;
+  if (t < tab.n_seg) cnt = tab.heads * ((tab.seg[t].y + 255) >> 8);
+  end[t] = cnt;
+  __syncthreads();
+  for (int d = 1; d < kNoAllocMaxSegments; d <<= 1) {
+    const int add = t >= d ? end[t - d] : 0;
+    __syncthreads();
+    end[t] += add;
+    __syncthreads();
+  }
+  for (int i = t; i < tab.n_items; i += blockDim.x) {
+    int lo = 0, hi = tab.n_seg - 1;            // first segment whose scan end exceeds i
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (end[mid] > i) hi = mid; else lo = mid + 1;
+    }
+    const int4 sg = tab.seg[lo];
+    const int r = i - (lo > 0 ? end[lo - 1] : 0);
+    const int chunks = (sg.y + 255) >> 8;
+    const int h = r / chunks, c = r - h * chunks;
+    AttnWork w;
+    w.q_row0 = sg.x + 256 * c;
+    w.q_len = min(256, sg.y - 256 * c);
+    w.k_row0 = sg.z;
+    w.k_len = sg.w;
+    w.head = h;
+    w.seg = tab.index[lo];
+    w.pad0 = w.pad1 = 0;
+    work[i] = w;
+  }
+}
+
 static std::mutex g_noalloc_mutex;
 static unsigned char* g_noalloc_dev[kNoAllocMaxDevices];        // device address of the array, per device ordinal
-static AttnWork g_noalloc_items[kNoAllocMaxItems];              // host staging of the work list (static, no heap)
-static int32_t g_noalloc_order[kNoAllocMaxSegments];
+
+// cuStreamGetDevice from the driver (CUDA 12.8 and later), fetched through the runtime; null when absent
+using StreamDeviceFn = CUresult (*)(CUstream, CUdevice*);
+static StreamDeviceFn stream_device_fn() {
+  static StreamDeviceFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamGetDevice", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<StreamDeviceFn>(p);
+  });
+  return fn;
+}
+
+// device memory (or managed memory) on device `dev`
+static bool on_device(const void* p, int dev) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) && a.device == dev;
+}
 
 }  // namespace orl
 
@@ -638,54 +720,58 @@ extern "C" int orl_attn_fwd_noalloc(const void* q, const void* k, const void* v,
   if (n_seg > 0 && (cu_q_host[n_seg] > nq || cu_k_host[n_seg] > nk)) return ORL_ERR_ARG;
   if (items > kNoAllocMaxItems) return ORL_ERR_CAPACITY;
 
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return ORL_ERR_LAUNCH;
-  if (g_noalloc_dev[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ORL_ERR_LAUNCH;
-    g_noalloc_dev[dev] = static_cast<unsigned char*>(p);
+  // the array's address below belongs to the current device: the tensors and the stream must live there too
+  if (items > 0 && nq > 0) {
+    if (!on_device(q, dev) || !on_device(out, dev) || (nk > 0 && (!on_device(k, dev) || !on_device(v, dev))) ||
+        (lse != nullptr && !on_device(lse, dev)))
+      return ORL_ERR_ARG;
   }
-  unsigned char* scratch = g_noalloc_dev[dev];
+  if (auto fn = stream_device_fn()) {
+    CUdevice sd = -1;
+    if (fn(reinterpret_cast<CUstream>(stream), &sd) == CUDA_SUCCESS && static_cast<int>(sd) != dev)
+      return ORL_ERR_ARG;
+  }
+
+  // the schedule of orl_attn_plan: segments with query rows by key count, descending (stable insertion sort)
+  NoAllocTable tab;
+  tab.n_seg = 0;
+  tab.heads = heads;
+  tab.n_items = static_cast<int>(items);
+  tab.pad = 0;
+  for (int i = 0; i < n_seg; ++i) {
+    const int lq = cu_q_host[i + 1] - cu_q_host[i];
+    if (lq == 0) continue;
+    const int lk = cu_k_host[i + 1] - cu_k_host[i];
+    int pos = tab.n_seg++;
+    while (pos > 0 && tab.seg[pos - 1].w < lk) {
+      tab.seg[pos] = tab.seg[pos - 1];
+      tab.index[pos] = tab.index[pos - 1];
+      --pos;
+    }
+    tab.seg[pos] = make_int4(cu_q_host[i], lq, cu_k_host[i], lk);
+    tab.index[pos] = i;
+  }
+
+  unsigned char* scratch;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_dev[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ORL_ERR_LAUNCH;
+      g_noalloc_dev[dev] = static_cast<unsigned char*>(p);
+    }
+    scratch = g_noalloc_dev[dev];
+  }
   int* err_dev = reinterpret_cast<int*>(scratch);
   AttnWork* work_dev = reinterpret_cast<AttnWork*>(scratch + kNoAllocHeaderBytes);
 
-  // the same schedule as orl_attn_plan: segments by key count, descending (stable insertion sort into a static
-  // buffer), items of one (segment, head) adjacent
-  int n_order = 0;
-  for (int i = 0; i < n_seg; ++i) {
-    if (cu_q_host[i + 1] == cu_q_host[i]) continue;
-    const int lk = cu_k_host[i + 1] - cu_k_host[i];
-    int pos = n_order++;
-    while (pos > 0 && cu_k_host[g_noalloc_order[pos - 1] + 1] - cu_k_host[g_noalloc_order[pos - 1]] < lk) {
-      g_noalloc_order[pos] = g_noalloc_order[pos - 1];
-      --pos;
-    }
-    g_noalloc_order[pos] = i;
-  }
-  int n = 0;
-  for (int o = 0; o < n_order; ++o) {
-    const int i = g_noalloc_order[o];
-    const int lq = cu_q_host[i + 1] - cu_q_host[i], lk = cu_k_host[i + 1] - cu_k_host[i];
-    for (int h = 0; h < heads; ++h)
-      for (int p = 0; p < lq; p += 256) {
-        AttnWork& w = g_noalloc_items[n++];
-        w.q_row0 = cu_q_host[i] + p;
-        w.q_len = std::min(256, lq - p);
-        w.k_row0 = cu_k_host[i];
-        w.k_len = lk;
-        w.head = h;
-        w.seg = i;
-        w.pad0 = w.pad1 = 0;
-      }
-  }
-  if (cudaMemsetAsync(err_dev, 0, sizeof(int), stream) != cudaSuccess) return ORL_ERR_LAUNCH;
+  // clears the error word and writes the work list (also when there is no work, so status reads 0)
+  noalloc_expand_kernel<<<1, 1024, 0, stream>>>(tab, work_dev, err_dev);
+  if (cudaGetLastError() != cudaSuccess) return ORL_ERR_LAUNCH;
   int rc = ORL_OK;
-  if (n > 0 && nq > 0) {
-    // pageable source: the call returns once the host buffer has been staged, so the next call may reuse it
-    if (cudaMemcpyAsync(work_dev, g_noalloc_items, static_cast<size_t>(n) * sizeof(AttnWork), cudaMemcpyHostToDevice,
-                        stream) != cudaSuccess)
-      return ORL_ERR_LAUNCH;
+  if (items > 0 && nq > 0) {
     const void* kk = k;
     const void* vv = v;
     long long nkk = nk;
@@ -693,6 +779,7 @@ extern "C" int orl_attn_fwd_noalloc(const void* q, const void* k, const void* v,
       kk = vv = q;
       nkk = nq;
     }
+    const int n = static_cast<int>(items);
     rc = head_dim == 64 ? launch_attn<64>(q, kk, vv, out, lse, nq, nkk, heads, scale, work_dev, n, err_dev, stream)
                         : launch_attn<128>(q, kk, vv, out, lse, nq, nkk, heads, scale, work_dev, n, err_dev, stream);
     if (rc != ORL_OK) return rc;

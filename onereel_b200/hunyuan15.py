@@ -78,6 +78,18 @@ class Context:
         return S.text_ranges(self.counts[self.cond()])
 
 
+# Optional phase timing for benchmarks: when PHASES is a list, Processor.scene / ulysses append (name, event) pairs,
+# each event recorded on the current stream at the end of the named phase (the first one, 'start', at its beginning).
+PHASES = None
+
+
+def _mark(name: str) -> None:
+    if PHASES is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        PHASES.append((name, e))
+
+
 def _layout_key(lay: SceneLayout):
     return (tuple(lay.lengths), lay.halo, lay.sides, tuple((j, tuple(sorted(v))) for j, v in sorted(lay.extra.items())))
 
@@ -349,6 +361,7 @@ class Processor:
         H, Dh = q.shape[1:]
         lse_overlap = ctx.overlap == 'lse'
         plan = self._plan(H, Dh, q.device, lse_overlap)
+        _mark('start')
         ex = comm.HaloExchange(ctx.layout, ctx.own, ctx.T, k, v) if D.world() > 1 else None
         if ex is not None and ex.remote_index != plan.remote_index:
             raise RuntimeError('exchange layout differs from the compiled plan')
@@ -356,17 +369,21 @@ class Processor:
             raise NotImplementedError("overlap='lse' with shared_pos='adjacent' is not on the B200 path")
         ov, ot = torch.empty_like(q), torch.zeros_like(eq)
         _attend(plan.near, q, eq, k, v, ek, ev, ov, ot, ctx=ctx)
+        _mark('near')
         if plan.lse:
             self._far_lse(plan, ex, q, eq, k, v, ek, ev, ov, ot)
         else:
             if ex is not None:
                 ex.wait()
+            _mark('exchange_wait')
             _attend(plan.far, q, eq, k, v, ek, ev, ov, ot, ex.remote_k if ex else None, ex.remote_v if ex else None,
                     ctx=ctx)
+            _mark('far')
         if ctx.text_sync == 'all_reduce' or D.world() == 1:
             D.all_reduce(ot)
         else:
             comm.send_text_rows(ot, ctx.layout, ctx.own, ctx.T, ctx.text_ranges())
+        _mark('text_sync')
         return ov, ot
 
     def _far_lse(self, plan, ex, q, eq, k, v, ek, ev, ov, ot):
@@ -376,8 +393,10 @@ class Processor:
         lse_v = torch.empty(H, q.shape[0], dtype=torch.float32, device=q.device)
         lse_t = torch.empty(H, eq.shape[0], dtype=torch.float32, device=q.device)
         _attend(plan.far_local, q, eq, k, v, ek, ev, ov, ot, lse_v=lse_v, lse_t=lse_t)
+        _mark('far_local')
         if ex is not None:
             ex.wait()
+        _mark('exchange_wait')
         fr = plan.far_remote
         if fr is None or not fr.segs:
             return
@@ -391,6 +410,7 @@ class Processor:
                 A.lse_merge(ov[lo:hi], lse_v[:, lo:hi], o2v[lo:hi], l2v[:, lo:hi])
             else:
                 A.lse_merge(ot[lo:hi], lse_t[:, lo:hi], o2t[lo:hi], l2t[:, lo:hi])
+        _mark('far_remote')
 
     def ulysses(self, q, k, v, eq, ek, ev):
         """hunyuan15.py:279-303: heads redistributed by all-to-all; every scene on the local heads; text outputs of the
@@ -398,8 +418,10 @@ class Processor:
         ctx = self.ctx
         n, r, H = D.world(), D.rank(), q.shape[1]
         sl = slice(r * H // n, (r + 1) * H // n)
+        _mark('start')
         qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
         eqs, eks, evs = (x[:, sl].contiguous() for x in (eq, ek, ev))
+        _mark('a2a_in')
         if ctx.attn_override is not None:
             res = ctx.attn_override(self.layer, qa, ka, va, eqs, eks, evs)
             if res is not None:
@@ -420,10 +442,14 @@ class Processor:
         ov = torch.empty_like(qa)
         otl = torch.zeros_like(eqs)
         _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl, ctx=ctx)
+        _mark('attention')
         ot = eq.new_zeros(eq.shape)
         ot[:, sl] = otl
         D.all_reduce(ot)
-        return comm.a2a_tokens(ov), ot
+        _mark('text_sync')
+        out = comm.a2a_tokens(ov)
+        _mark('a2a_out')
+        return out, ot
 
 
 def apply_rotary_emb(x, freqs):
