@@ -102,7 +102,8 @@ def rope_3d(frames: int, h: int, w: int, head_dim: int = 128, axes=(16, 56, 56),
 def build(ctx: HY.Context, device, dim=2048, heads=16, blocks=54, seed=0) -> Transformer:
     """the stand-in with a B200 Processor on every block (hunyuan15.install's attention part)"""
     torch.manual_seed(seed)
-    model = Transformer(dim, heads, blocks).to(device, torch.bfloat16)
+    with torch.device(device):                   # parameters created and initialised on the GPU
+        model = Transformer(dim, heads, blocks).to(torch.bfloat16)
     for p in model.parameters():
         nn.init.normal_(p, std=0.02) if p.dim() > 1 else nn.init.zeros_(p)
     for blk in model.transformer_blocks:
