@@ -153,6 +153,29 @@ ORL_API int orl_qk_norm_rope(const void* x, void* y, const void* weight, const f
 ORL_API int orl_rope_rows(void* x, const int32_t* rows, long long n_rows, int heads, int head_dim, const float* cos_t,
                           const float* sin_t, long long rope_ld, int sin_shift, void* stream);
 
+/* ---------------------------------------------------------------- frame memory (src/onereel/frame_memory.py) */
+
+/* Per-frame pooling of one layer's hidden states (frame_memory.py:76-85 `collect`, an index_add_ of the rows into
+ * per-frame sums and counts): acc[f * ld_acc + c] += sum of hs[row * ld_hs + c] over the rows of frame f and
+ * acc[f * ld_acc + C] += their number. Rows in CSR form: rows_by_frame[frame_off[f] .. frame_off[f + 1]] (device
+ * int32; rows of no frame are simply not listed). hs: bf16 (dtype 0) or fp32 (dtype 1), C a multiple of 8, rows
+ * 16-byte aligned; acc fp32 with ld_acc >= C + 1. Deterministic (fixed summation order, no atomics). */
+ORL_API int orl_frame_pool(const void* hs, int dtype, long long ld_hs, int C, const int32_t* rows_by_frame,
+                           const int32_t* frame_off, int n_frames, float* acc, long long ld_acc, void* stream);
+
+/* fp32 elements of scratch orl_frame_select needs per set. */
+ORL_API long long orl_frame_select_scratch(int C, int n_cand, int k);
+
+/* Representative frames by cosine k-means (frame_memory.py:87-132 `finish` + `select`), for n_sets feature sets at
+ * once (one per observed layer; set s at feat + s * set_stride, fp32 rows of stride ld). normalize = 1: rows hold
+ * [sums (C), count] and the candidate rows are first replaced by their L2-normalised means (in place); 0: rows are
+ * already normalised features. cand: device int32 [n_cand] candidate frames; k clusters (1..min(n_cand, 64)), at
+ * most `iters` Lloyd steps. reps: device int32 [n_sets, k + 1]: the number of representatives n, then n frame
+ * indices ascending (-1 after). scratch: device fp32, scratch_stride >= orl_frame_select_scratch per set. */
+ORL_API int orl_frame_select(float* feat, long long ld, long long set_stride, int n_sets, int C, int normalize,
+                             const int32_t* cand, int n_cand, int k, int iters, float* scratch,
+                             long long scratch_stride, int32_t* reps, void* stream);
+
 /* ---------------------------------------------------------------- native planner (comm.py:18-112, layout.py:54-78) */
 
 /* A scene layout (layout.py:10-18 SceneLayout): lengths[n_scenes] latent frames per scene, halo frames of the

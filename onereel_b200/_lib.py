@@ -70,6 +70,10 @@ SIGNATURES = {
     'orl_qk_norm_rope': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_int, c_int, c_int, c_float, c_int, c_ll, c_vp,
                                  c_vp]),
     'orl_rope_rows': (c_int, [c_vp, c_vp, c_ll, c_int, c_int, c_vp, c_vp, c_ll, c_int, c_vp]),
+    'orl_frame_pool': (c_int, [c_vp, c_int, c_ll, c_int, c_vp, c_vp, c_int, c_vp, c_ll, c_vp]),
+    'orl_frame_select_scratch': (c_ll, [c_int, c_int, c_int]),
+    'orl_frame_select': (c_int, [c_vp, c_ll, c_ll, c_int, c_int, c_int, c_vp, c_int, c_int, c_int, c_vp, c_ll, c_vp,
+                                 c_vp]),
     'orl_key_frames': (c_int, [c_vp, c_int, P_I32, c_int]),
     'orl_query_cost': (c_int, [c_vp, c_ll, P_I32, c_ll, ctypes.POINTER(ctypes.c_double)]),
     'orl_balanced': (c_int, [P_I64, ctypes.POINTER(ctypes.c_double), c_int, c_int, P_I64]),

@@ -10,6 +10,8 @@ checked against it:
                            the scene processors' outputs (reference: src/onereel/attention.py, which calls
                            flash-attn 2.8.3.post1 `flash_attn_varlen_func`; its published algorithm is exact softmax
                            attention, restated here directly)
+  oracle.frame_memory_oracle per-frame pooling and the cosine k-means choice of representative frames in float64
+                           numpy (reference: src/onereel/frame_memory.py)
 
 Only `tests/`, `__graft_entry__.smoke()` and `bench.py`'s CPU-baseline leg may import this package, and only as the
 checker or the timed CPU baseline. The product (`onereel_b200`) never imports it and has no CPU fallback.
