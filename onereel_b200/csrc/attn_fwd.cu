@@ -232,105 +232,128 @@ __device__ __forceinline__ void softmax_role(const AttnShared& sh, uint32_t tmem
   float m_run[2][2] = {{-INFINITY, -INFINITY}, {-INFINITY, -INFINITY}};
   float l_run[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   bool ok = n_kv > 0;
+  // One tile's softmax on the scores sv (already loaded and waited for): mask, max, exponentials, P in two halves.
+  // Everything up to the store of P's second half; finish_tile then waits for that store and hands it over.
+  struct TileState {
+    float m0, m1, l0, l1;
+  };
+  auto tile_front = [&](int j, int t, int valid, uint32_t (&sv)[64], uint32_t (&pb)[16]) -> TileState {
+    const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
+    if (valid < 128) {
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (8 * r + 2 * cq + (k & 1) >= valid) sv[4 * r + k] = __float_as_uint(-INFINITY);
+    }
+    auto tile_max = [&](int i) {
+      float a = __uint_as_float(sv[2 * i]), b = __uint_as_float(sv[2 * i + 1]);
+#pragma unroll
+      for (int r = 1; r < 16; r += 2) {
+        a = fmax3(a, __uint_as_float(sv[4 * r + 2 * i]), __uint_as_float(sv[4 * r + 2 * i + 1]));
+        if (r + 1 < 16) b = fmax3(b, __uint_as_float(sv[4 * (r + 1) + 2 * i]), __uint_as_float(sv[4 * (r + 1) + 2 * i + 1]));
+      }
+      return quad_max(fmaxf(a, b));
+    };
+    // exponentials of keys [64 h, 64 h + 64) of both rows against neg_i = -m_i * log2e * scale: P words for a
+    // 16x128b store (register 2r + i: row i, word 4r + cq) and the two rows' sums, each row's two keys summed as
+    // one f32x2 pair (half the add instructions)
+    auto exp_half = [&](int h, float neg0, float neg1, uint32_t (&p)[16], float& sum0, float& sum1) {
+      F2 acc0 = f2(0.f, 0.f), acc1 = f2(0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int base = 4 * (8 * h + r);
+        const float x0 = ex2(fmaf(__uint_as_float(sv[base + 0]), scale_log2, neg0));
+        const float x1 = ex2(fmaf(__uint_as_float(sv[base + 1]), scale_log2, neg0));
+        const float y0 = ex2(fmaf(__uint_as_float(sv[base + 2]), scale_log2, neg1));
+        const float y1 = ex2(fmaf(__uint_as_float(sv[base + 3]), scale_log2, neg1));
+        acc0 = fadd2(acc0, f2(x0, x1));
+        acc1 = fadd2(acc1, f2(y0, y1));
+        p[2 * r + 0] = pack_bf16x2(x0, x1);
+        p[2 * r + 1] = pack_bf16x2(y0, y1);
+      }
+      const float2 u0 = f2_split(acc0), u1 = f2_split(acc1);
+      sum0 = u0.x + u0.y;
+      sum1 = u1.x + u1.y;
+    };
+    float* mr = m_run[t];
+    float* lr = l_run[t];
+    float m_use0 = mr[0], m_use1 = mr[1];
+    uint32_t pa[16];
+    float sa0, sa1;
+    if (j == 0) {
+      m_use0 = tile_max(0);
+      m_use1 = tile_max(1);
+      exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
+    } else {
+      exp_half(0, -mr[0] * scale_log2, -mr[1] * scale_log2, pa, sa0, sa1);   // speculative
+      const float mx0 = tile_max(0), mx1 = tile_max(1);
+      const bool redo0 = (mx0 - mr[0]) * scale_log2 > kMaxJump, redo1 = (mx1 - mr[1]) * scale_log2 > kMaxJump;
+      if (__any_sync(0xffffffffu, redo0 || redo1)) {
+        // the warp redoes its tile together (TMEM loads and stores are warp-wide), but only rows whose max jumped
+        // take the new max: the others keep theirs (factor exactly 1, P unchanged), so a row's result never
+        // depends on which rows share its warp or work item
+        m_use0 = redo0 ? fmaxf(mr[0], mx0) : mr[0];
+        m_use1 = redo1 ? fmaxf(mr[1], mx1) : mr[1];
+        const float al0 = redo0 ? ex2((mr[0] - m_use0) * scale_log2) : 1.0f;
+        const float al1 = redo1 ? ex2((mr[1] - m_use1) * scale_log2) : 1.0f;
+        exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
+        lr[0] *= al0;
+        lr[1] *= al1;
+        const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
+#pragma unroll
+        for (int ch = 0; ch < D / 64; ++ch) {
+          uint32_t o[32];
+          tmem_ld_16x256b_x8(o_addr + 64 * ch, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * ((e & 2) ? al1 : al0));
+          tmem_st_16x256b_x8(o_addr + 64 * ch, o);
+        }
+      }
+    }
+    tmem_st_16x128b_x8(s_addr, pa);
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(sh.bar(C::kBarP + 2 * t + 0));
+    float sb0, sb1;
+    exp_half(1, -m_use0 * scale_log2, -m_use1 * scale_log2, pb, sb0, sb1);
+    tmem_st_16x128b_x8(s_addr + 32, pb);
+    return TileState{m_use0, m_use1, sa0 + sb0, sa1 + sb1};
+  };
+  auto tile_back = [&](int t, const TileState& st) {
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(sh.bar(C::kBarP + 2 * t + 1));
+    l_run[t][0] += st.l0;
+    l_run[t][1] += st.l1;
+    m_run[t][0] = st.m0;
+    m_run[t][1] = st.m1;
+  };
+  auto load_s = [&](int t, uint32_t (&sv)[64]) {
+    const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
+    tmem_ld_16x256b_x8(s_addr, sv);
+    tmem_ld_16x256b_x8(s_addr + 64, sv + 32);
+  };
+  uint32_t s[64], s2[64];                      // s[4r + 2i + e]: row i, key 8r + 2 cq + e
+  uint32_t pb[16];
   for (int j = 0; ok && j < n_kv; ++j) {
     const int valid = wi.k_len - 128 * j;
-    for (int t = 0; t < n_qt; ++t) {
-      ok = mbar_wait(sh.bar(C::kBarS + t), j & 1, sh.abort_flag);
+    ok = mbar_wait(sh.bar(C::kBarS + 0), j & 1, sh.abort_flag);
+    if (!ok) break;
+    tc_fence_after();
+    load_s(0, s);
+    tmem_wait_ld();
+    const TileState st0 = tile_front(j, 0, valid, s, pb);
+    tile_back(0, st0);
+    if (n_qt == 2) {
+      ok = mbar_wait(sh.bar(C::kBarS + 1), j & 1, sh.abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t s_addr = tmem + C::col_s(t) + lane_off;
-      uint32_t s[64];                          // s[4r + 2i + e]: row i, key 8r + 2 cq + e
-      tmem_ld_16x256b_x8(s_addr, s);
-      tmem_ld_16x256b_x8(s_addr + 64, s + 32);
+      load_s(1, s2);
       tmem_wait_ld();
-      if (valid < 128) {
-#pragma unroll
-        for (int r = 0; r < 16; ++r)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (8 * r + 2 * cq + (k & 1) >= valid) s[4 * r + k] = __float_as_uint(-INFINITY);
-      }
-      auto tile_max = [&](int i) {
-        float a = __uint_as_float(s[2 * i]), b = __uint_as_float(s[2 * i + 1]);
-#pragma unroll
-        for (int r = 1; r < 16; r += 2) {
-          a = fmax3(a, __uint_as_float(s[4 * r + 2 * i]), __uint_as_float(s[4 * r + 2 * i + 1]));
-          if (r + 1 < 16) b = fmax3(b, __uint_as_float(s[4 * (r + 1) + 2 * i]), __uint_as_float(s[4 * (r + 1) + 2 * i + 1]));
-        }
-        return quad_max(fmaxf(a, b));
-      };
-      // exponentials of keys [64 h, 64 h + 64) of both rows against neg_i = -m_i * log2e * scale: P words for a
-      // 16x128b store (register 2r + i: row i, word 4r + cq) and the two rows' sums
-      auto exp_half = [&](int h, float neg0, float neg1, uint32_t (&p)[16], float& sum0, float& sum1) {
-        float a0 = 0.f, b0 = 0.f, a1 = 0.f, b1 = 0.f;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const int base = 4 * (8 * h + r);
-          const float x0 = ex2(fmaf(__uint_as_float(s[base + 0]), scale_log2, neg0));
-          const float x1 = ex2(fmaf(__uint_as_float(s[base + 1]), scale_log2, neg0));
-          const float y0 = ex2(fmaf(__uint_as_float(s[base + 2]), scale_log2, neg1));
-          const float y1 = ex2(fmaf(__uint_as_float(s[base + 3]), scale_log2, neg1));
-          a0 += x0;
-          b0 += x1;
-          a1 += y0;
-          b1 += y1;
-          p[2 * r + 0] = pack_bf16x2(x0, x1);
-          p[2 * r + 1] = pack_bf16x2(y0, y1);
-        }
-        sum0 = a0 + b0;
-        sum1 = a1 + b1;
-      };
-      float* mr = m_run[t];
-      float* lr = l_run[t];
-      float m_use0 = mr[0], m_use1 = mr[1];
-      uint32_t pa[16];
-      float sa0, sa1;
-      if (j == 0) {
-        m_use0 = tile_max(0);
-        m_use1 = tile_max(1);
-        exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
-      } else {
-        exp_half(0, -mr[0] * scale_log2, -mr[1] * scale_log2, pa, sa0, sa1);   // speculative
-        const float mx0 = tile_max(0), mx1 = tile_max(1);
-        const bool redo0 = (mx0 - mr[0]) * scale_log2 > kMaxJump, redo1 = (mx1 - mr[1]) * scale_log2 > kMaxJump;
-        if (__any_sync(0xffffffffu, redo0 || redo1)) {
-          // the warp redoes its tile together (TMEM loads and stores are warp-wide), but only rows whose max jumped
-          // take the new max: the others keep theirs (factor exactly 1, P unchanged), so a row's result never
-          // depends on which rows share its warp or work item
-          m_use0 = redo0 ? fmaxf(mr[0], mx0) : mr[0];
-          m_use1 = redo1 ? fmaxf(mr[1], mx1) : mr[1];
-          const float al0 = redo0 ? ex2((mr[0] - m_use0) * scale_log2) : 1.0f;
-          const float al1 = redo1 ? ex2((mr[1] - m_use1) * scale_log2) : 1.0f;
-          exp_half(0, -m_use0 * scale_log2, -m_use1 * scale_log2, pa, sa0, sa1);
-          lr[0] *= al0;
-          lr[1] *= al1;
-          const uint32_t o_addr = tmem + C::col_o(t) + lane_off;
-#pragma unroll
-          for (int ch = 0; ch < D / 64; ++ch) {
-            uint32_t o[32];
-            tmem_ld_16x256b_x8(o_addr + 64 * ch, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * ((e & 2) ? al1 : al0));
-            tmem_st_16x256b_x8(o_addr + 64 * ch, o);
-          }
-        }
-      }
-      tmem_st_16x128b_x8(s_addr, pa);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(sh.bar(C::kBarP + 2 * t + 0));
-      uint32_t pb[16];
-      float sb0, sb1;
-      exp_half(1, -m_use0 * scale_log2, -m_use1 * scale_log2, pb, sb0, sb1);
-      tmem_st_16x128b_x8(s_addr + 32, pb);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(sh.bar(C::kBarP + 2 * t + 1));
-      lr[0] += sa0 + sb0;
-      lr[1] += sa1 + sb1;
-      mr[0] = m_use0;
-      mr[1] = m_use1;
+      const TileState st1 = tile_front(j, 1, valid, s2, pb);
+      tile_back(1, st1);
     }
   }
   if (ok) ok = mbar_wait(sh.bar(C::kBarDone), 0, sh.abort_flag);

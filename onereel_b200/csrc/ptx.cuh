@@ -285,6 +285,26 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// ---- packed FP32 pairs (sm_100's .f32x2 instructions: one issue slot for two lanes' worth of FP32 adds)
+struct F2 {
+  uint64_t v;
+};
+__device__ __forceinline__ F2 f2(float lo, float hi) {
+  F2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(F2 a) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(a.v));
+  return r;
+}
+__device__ __forceinline__ F2 fadd2(F2 a, F2 b) {
+  F2 d;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+  return d;
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

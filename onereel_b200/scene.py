@@ -163,7 +163,9 @@ def remote_index_of(layout, T, own_all, r, needed_fn):
 @dataclass
 class ScenePlan:
     """compiled segments of one packed call on one device: K/V run table (slots VIDEO, TEXT, REMOTE -> slot 3 =
-    packed buffer), query rows in place per segment, the attention work list, cu_seqlens"""
+    packed buffer), query rows in place per segment, the attention work list, cu_seqlens (host lists cu_q / cu_k;
+    cu_k_dev: the packed K/V's cu_seqlens_k as the reference's int32 device tensor, attention.py:28-29, written by
+    every pack_kv launch)"""
     segs: list
     row_bytes: int
     heads: int
@@ -174,6 +176,8 @@ class ScenePlan:
     lk: list = field(default_factory=list)
     cu_q: list = field(default_factory=list)
     cu_k: list = field(default_factory=list)
+    cu_k_dev: torch.Tensor = None
+    lk_dev: torch.Tensor = None
 
     def __post_init__(self):
         rb = self.row_bytes
@@ -193,9 +197,12 @@ class ScenePlan:
         self.lk = [s.lk for s in self.segs]
         self.cu_q = np.concatenate([[0], np.cumsum(self.lq)]).astype(np.int32).tolist()
         self.cu_k = np.concatenate([[0], np.cumsum(self.lk)]).astype(np.int32).tolist()
+        self.lk_dev = torch.tensor(self.lk, dtype=torch.int32, device=self.device)
+        self.cu_k_dev = torch.empty(len(self.lk) + 1, dtype=torch.int32, device=self.device)
 
     def pack_kv(self, k_video, v_video, k_text, v_text, k_remote=None, v_remote=None, out=None):
-        """one pack launch for K and V (two planes): returns packed (k, v) [n_keys, H, D]"""
+        """one pack launch for K and V (two planes): returns packed (k, v) [n_keys, H, D]; the same launch writes
+        cu_k_dev"""
         H, Dh = k_video.shape[1:]
         if out is None:
             kp = k_video.new_empty(self.n_keys, H, Dh)
@@ -205,7 +212,7 @@ class ScenePlan:
         ptr = lambda x: 0 if x is None else x.data_ptr()
         src = [ptr(k_video), ptr(k_text), ptr(k_remote), 0, ptr(v_video), ptr(v_text), ptr(v_remote), 0]
         dst = [0, 0, 0, kp.data_ptr(), 0, 0, 0, vp.data_ptr()]
-        self.kv_table.run(src, dst, n_planes=2)
+        self.kv_table.run(src, dst, n_planes=2, seg_len_dev=self.lk_dev, cu_out=self.cu_k_dev)
         return kp, vp
 
 

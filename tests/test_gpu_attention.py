@@ -187,8 +187,10 @@ def test_cfg2_full_size_sampled_rows():
     assert mx < MAX_ABS and mean < MEAN_ABS and lmx < 1e-3, (mx, mean, lmx)
 
 
-def test_ring_single_rank_matches_scene_path():
-    """the Scene-Ring path on one rank (one step, LSE merge into the fp32 accumulator) against the scene path"""
+def test_ring_single_rank_matches_oracle():
+    """the Scene-Ring path on one rank (one step: pack, attention with LSE, LSE merge into the fp32 accumulator)
+    against the CPU oracle of the reference's scene attention (hunyuan15.Processor.scene), within the kernel
+    tolerance"""
     from onereel_b200 import hunyuan15 as HY, ring as R
     from onereel_b200.layout import SceneLayout
     lay = SceneLayout([3, 5, 2], halo=1, extra={0: [7], 2: [0]})
@@ -197,10 +199,14 @@ def test_ring_single_rank_matches_scene_path():
     q, k, v = rand(L, H, Dh, seed=1), rand(L, H, Dh, seed=2), rand(L, H, Dh, seed=3)
     eq, ek, ev = rand(17, H, Dh, seed=4), rand(17, H, Dh, seed=5), rand(17, H, Dh, seed=6)
     ctx = HY.Context(lay, T=T, counts={True: counts}, fwd=1, own=[(0, L)])
-    ref_v, ref_t = HY.Processor(ctx, 0).scene(q, k, v, eq, ek, ev)
     plan = R.RingPlan(lay, 1, T)
     rows = plan.perm
     ov, ot = R.attention(plan, q[rows].contiguous(), k[rows].contiguous(), v[rows].contiguous(), eq, ek, ev,
                          ctx.text_ranges(), id(lay.extra))
-    rel = lambda x, y: ((x.float() - y.float()).norm() / y.float().norm()).item()
-    assert rel(ov, ref_v[rows]) < 1e-2 and rel(ot, ref_t) < 1e-2
+    torch.cuda.synchronize()
+    olay = LO.Layout([3, 5, 2], halo=1, extra={0: [7], 2: [0]})
+    want_v, want_t, _ = AO.hunyuan_scene(olay, T, counts, *(x.float().cpu().numpy() for x in (q, k, v, eq, ek, ev)))
+    dv = np.abs(ov.float().cpu().numpy() - want_v[rows.cpu().numpy()])
+    dt = np.abs(ot.float().cpu().numpy() - want_t)
+    d = np.concatenate([dv.ravel(), dt.ravel()])
+    assert d.max() < MAX_ABS and d.mean() < MEAN_ABS, (d.max(), d.mean())
