@@ -61,7 +61,7 @@ TRAFFIC_PER_ALG_BYTE = 373.86 / 392.9
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3          # north_star's tolerance on bf16 inputs
 # NVLink 5 peer copy per direction per GPU, as measured on this pool's B200 nodes (nominal 900 GB/s)
 NVLINK_PEER_GBS = 770.0
-LEGS = ('parity', 'phases', 'comm', 'cfg3', 'dit', 'fa2')
+LEGS = ('parity', 'phases', 'comm', 'kernels', 'cfg3', 'dit', 'fa2')
 
 
 def cfg_layout(cfg):
@@ -514,6 +514,70 @@ def e2e_leg(lb, steps):
 
 # ------------------------------------------------------------------------------------------------ legs
 
+def kernels_leg(lb, dev, warmup=3, steps=10):
+    """the HBM-bound kernels of the path on the cfg2 layer, each timed alone with CUDA events on its stream (inputs
+    larger than L2), against the measured copy bandwidth: the K/V pack, the fused q/k RMSNorm + RoPE, the two LSE
+    merges, the frame-memory pooling. bytes = algorithmic bytes per launch (every byte the kernel must read and
+    write once)."""
+    from onereel_b200 import attention as A, frame_memory as FM, rope
+    from onereel_b200.layout import SceneLayout
+    _, _, hbm, kind = peaks()
+    stream = torch.cuda.current_stream(dev)
+    q, k, v, eq, ek, ev = lb.inputs
+    H, Dh = lb.H, lb.Dh
+    plan = lb.proc._plan(H, Dh, dev, False).near
+    res = {}
+
+    def timed(name, fn, nbytes, what):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = dict(ms=ms, bytes=nbytes, achieved_gbs=gbs, peak_gbs=hbm, frac=gbs / hbm, what=what)
+
+    kp, vp = plan.pack_kv(k, v, ek, ev)
+    timed('pack', lambda: plan.pack_kv(k, v, ek, ev, out=(kp, vp)), 2 * 2 * kp.numel() * 2,
+          'orl_pack: K and V of every cfg2 segment gathered into the packed layout (read + write of every key row)')
+    del kp, vp
+    rows = q.shape[0]
+    x = q.reshape(rows, H * Dh)
+    w = torch.ones(Dh, dtype=torch.bfloat16, device=dev)
+    cos = torch.rand(rows, Dh, device=dev)
+    sin = torch.rand(rows, Dh, device=dev)
+    y = torch.empty_like(q)
+    timed('qk_norm_rope', lambda: rope.qk_norm_rope(x, w, cos, sin, H, 1e-6, True, 0, out=y),
+          rows * H * Dh * 2 * 2 + rows * Dh * 4 * 2,
+          "orl_qk_norm_rope on the layer's video rows (Hunyuan per-head RMSNorm + RoPE): read x, cos, sin; write y")
+    del y, cos, sin
+    n = rows
+    o1, o2 = q.clone(), k.clone()
+    l1 = torch.randn(H, n, device=dev)
+    l2 = torch.randn(H, n, device=dev)
+    timed('lse_merge', lambda: A.lse_merge(o1, l1, o2, l2), 3 * n * H * Dh * 2 + 3 * n * H * 4,
+          "orl_lse_merge of two bf16 partial outputs of the layer's video rows (read o1, o2, both lse; write o1, lse)")
+    acc = o1.float()
+    del o1
+    timed('lse_merge_acc', lambda: A.lse_merge_acc(acc, l1, o2, l2),
+          2 * n * H * Dh * 4 + n * H * Dh * 2 + 3 * n * H * 4,
+          'orl_lse_merge_acc into an fp32 accumulator (Scene-Ring step): read + write acc, read the bf16 part')
+    del acc, o2
+    C = 2048
+    hs = torch.randn(n, C, device=dev).to(torch.bfloat16)
+    frame = (torch.arange(n, device=dev) // lb.T).to(torch.int64)
+    fm = FM.FrameMemory(budget=4)
+    fm.reset(SceneLayout(list(lb.lay.lengths), halo=0), n_layers=1)
+    timed('frame_pool', lambda: fm.collect(frame, hs, layer=0), n * C * 2,
+          "orl_frame_pool: per-frame sums of one layer's hidden states [rows, 2048] bf16 (read once)")
+    return dict(kernels=res, peak_source=f'{kind} HBM copy bandwidth ({hbm:.0f} GB/s)')
+
+
 def fa2_leg(dev, warmup=3, steps=10):
     """the reference's own GPU kernel on the same packed cfg2 segments, for a GPU-to-GPU comparison: FlashAttention-2
     2.8.3 varlen (src/onereel/attention.py:39-43 with BACKEND 'fa2'), against this kernel on the same packed q / k / v;
@@ -727,6 +791,8 @@ def run_headline(args, dev, rank, world, local):
                    h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
                    note='processor call with pinned H2D inputs / D2H outputs every step; consecutive steps '
                         'pipelined on separate copy streams (double-buffered inputs)')
+    if 'kernels' in legs and world == 1:
+        extra['hbm_kernels'] = kernels_leg(lb, dev)
     run_mode, path, own = lb.ctx.run_mode, lb.ctx.path, lb.ctx.own
     layout = dict(cfg, scenes=lb.lay.n_scenes)
     del lb

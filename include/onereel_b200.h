@@ -118,12 +118,13 @@ ORL_API long long orl_pack_prepare(orl_copy_run* runs, const int64_t* nbytes, in
 
 /* Gather/pack kernel: executes the prepared run table (device copy, runs_dev [n_runs]) for `n_planes` planes at
  * once (e.g. K and V share one run table): plane p reads src_bases[p * n_slots + slot] and writes
- * dst_bases[p * n_slots + slot]. Coalesced 16-byte vector copies, HBM-bound. When cu_out_dev is not NULL, also
- * writes cu_seqlens: cu_out_dev[0 .. n_seg] = [0, cumsum(seg_len_dev)] (int32, attention.py:28-29).
+ * dst_bases[p * n_slots + slot]. TMA bulk copies staged through shared memory, HBM-bound. When cu_out_dev is not
+ * NULL, also writes cu_seqlens: cu_out_dev[0 .. n_seg] = [0, cumsum(seg_len_dev)] (int32, attention.py:28-29).
+ * err_dev (optional device int): a bounded wait that gave up ORs its bit in (see orl_error_bits_describe).
  * At most 8 slots and 3 planes. */
 ORL_API int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_vecs, int n_planes, int n_slots,
              const void* const* src_bases, void* const* dst_bases, const int32_t* seg_len_dev, int n_seg,
-             int32_t* cu_out_dev, void* stream);
+             int32_t* cu_out_dev, int* err_dev, void* stream);
 
 /* Log-sum-exp merge of two partial attention results over disjoint key sets (hunyuan15.py:274-276, ring.py:63-70):
  * o1 [n, heads, head_dim] bf16 (in/out) with its lse1 [heads, ld_lse1] fp32 (in/out), o2 / lse2 [heads, ld_lse2]

@@ -64,7 +64,7 @@ SIGNATURES = {
     'orl_attn_fwd_noalloc': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_int, c_int, c_float, P_I32, P_I32,
                                      c_int, c_vp, c_vp]),
     'orl_pack_prepare': (c_ll, [c_vp, P_I64, c_int]),
-    'orl_pack': (c_int, [c_vp, c_int, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp]),
+    'orl_pack': (c_int, [c_vp, c_int, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
     'orl_lse_merge': (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_ll, c_int, c_int, c_vp]),
     'orl_lse_merge_acc': (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_ll, c_int, c_int, c_vp]),
     'orl_qk_norm_rope': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_int, c_int, c_int, c_float, c_int, c_ll, c_vp,

@@ -31,6 +31,7 @@ extern "C" int orl_error_bits_describe(int bits, char* buf, int cap) {
       {orl::kErrTimeoutMma, "MMA warp timed out waiting for a tile or for P"},
       {orl::kErrTimeoutSoftmax, "softmax warps timed out waiting for S or O"},
       {orl::kErrTimeoutDrain, "wind-down timed out waiting for in-flight copies"},
+      {orl::kErrTimeoutPack, "pack kernel timed out waiting for a bulk copy"},
   };
   int n = 0;
   for (const auto& e : names)

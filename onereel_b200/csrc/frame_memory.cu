@@ -61,7 +61,21 @@ __global__ void __launch_bounds__(256) frame_pool_kernel(const T* __restrict__ h
   const int r0 = frame_off[f], r1 = frame_off[f + 1];
   float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (col < C) {
-    for (int i = r0 + ty; i < r1; i += kPoolRowLanes) {
+    // rows i, i + 32, i + 64, ... of the frame, added in that order; four rows' loads in flight at a time
+    int i = r0 + ty;
+    for (; i + 3 * kPoolRowLanes < r1; i += 4 * kPoolRowLanes) {
+      int idx[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) idx[u] = __ldg(&rows_by_frame[i + u * kPoolRowLanes]);
+      float v[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load8<T>(hs + static_cast<long long>(idx[u]) * ld_hs + col, v[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s[e] += v[u][e];
+    }
+    for (; i < r1; i += kPoolRowLanes) {
       float v[8];
       load8<T>(hs + static_cast<long long>(rows_by_frame[i]) * ld_hs + col, v);
 #pragma unroll

@@ -3,26 +3,31 @@
 // orl_pack executes a prepared run table: every run copies one contiguous byte range (a run of rows) from a source
 // base to a destination base. It replaces the torch.cat copies that assemble each packed segment of the reference
 // (src/onereel/attention.py:60-61, 69; src/onereel/models/hunyuan15.py:164, 168, 225; parallel/comm.py:200) and the
-// scatter of outputs back to token rows (hunyuan15.py:231-235; wan.py:117-118). All runs of a plane (e.g. K, then V
-// sharing the same table) are one flat space of 16-byte vectors cut into tiles of kPackTile vectors; a block takes
-// tiles in a grid-stride loop, finds the run of the tile's first vector once (binary search over the runs' vector
-// prefix, uniform across the block), and each thread then copies kPackUnroll vectors of the tile, consecutive
-// threads on consecutive 16-byte vectors (coalesced), all loads issued before the stores. A thread's run index only
-// moves forward inside a tile (runs are at least one 16-byte vector, usually whole rows of kilobytes).
+// scatter of outputs back to token rows (hunyuan15.py:231-235; wan.py:117-118). The copies run on the TMA engine as
+// untiled bulk copies staged through shared memory: all runs of a plane (e.g. K, then V sharing the same table) are
+// one flat byte space cut into tiles of kPackTile bytes; a CTA (one per SM, one issuing thread) takes tiles in a
+// grid-stride loop, cuts each into pieces of at most kPackStage bytes that stay inside one run, and keeps a ring of
+// kPackStages pieces in flight: bulk load global -> shared (completion on the stage's mbarrier), then, kPackLag
+// pieces later, bulk store shared -> global; a stage is reloaded once its store has finished reading it. Every byte
+// crosses HBM once each way and no thread touches the data.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 #include "orl_common.h"
+#include "ptx.cuh"
 
 namespace orl {
 
-constexpr int kPackThreads = 256;
-constexpr int kPackUnroll = 8;
-constexpr int kPackTile = kPackThreads * kPackUnroll;   // 2048 vectors = 32 KiB per tile
+constexpr int kPackStages = 6;
+constexpr int kPackLag = 3;                          // stores trail loads by this many pieces
+constexpr int kPackStage = 32 * 1024;                // bytes per piece / shared-memory stage
+constexpr long long kPackTile = 256 * 1024;          // bytes per grid-stride tile
+constexpr int kPackSmem = kPackStages * kPackStage + kPackStages * 8 + 16;
 constexpr int kMaxSlots = 8;
 constexpr int kMaxPlanes = 3;
+static_assert(kPackLag < kPackStages, "a stage must be stored before it is reloaded");
 
 struct PackBases {
   const uint8_t* src[kMaxPlanes * kMaxSlots];
@@ -39,12 +44,13 @@ __device__ __forceinline__ int find_run(const CopyRun* __restrict__ runs, int n_
   return lo;
 }
 
-__global__ void __launch_bounds__(kPackThreads) pack_kernel(const CopyRun* __restrict__ runs, int n_runs,
-                                                            long long total_vecs, long long tiles_per_plane,
-                                                            int n_planes, int n_slots, PackBases bases,
-                                                            const int32_t* __restrict__ seg_len, int n_seg,
-                                                            int32_t* __restrict__ cu_out) {
-  if (cu_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
+__global__ void __launch_bounds__(32) pack_kernel(const CopyRun* __restrict__ runs, int n_runs,
+                                                  long long total_bytes, long long tiles_per_plane, int n_planes,
+                                                  int n_slots, PackBases bases, const int32_t* __restrict__ seg_len,
+                                                  int n_seg, int32_t* __restrict__ cu_out, int* __restrict__ err) {
+  extern __shared__ __align__(128) uint8_t pack_smem[];
+  if (threadIdx.x != 0) return;
+  if (cu_out != nullptr && blockIdx.x == 0) {
     int32_t acc = 0;
     cu_out[0] = 0;
     for (int i = 0; i < n_seg; ++i) {
@@ -52,35 +58,71 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const CopyRun* __res
       cu_out[i + 1] = acc;
     }
   }
+  const uint32_t stage0 = smem_u32(pack_smem);
+  const uint32_t bar0 = stage0 + kPackStages * kPackStage;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(pack_smem + kPackStages * kPackStage + kPackStages * 8);
+  *abort_flag = 0;
+  for (int st = 0; st < kPackStages; ++st) mbar_init(bar0 + 8u * st, 1);
+  fence_mbar_init();
+  const uint64_t pol = policy_evict_first();         // sources are read once
+  uint8_t* pdst[kPackStages] = {};                   // destination and size of the piece in each stage
+  uint32_t pbytes[kPackStages] = {};
+  long long issued = 0, stored = 0;                  // pieces loaded / stored
+  bool ok = true;
+  auto store = [&](long long j) -> bool {
+    const int st = static_cast<int>(j % kPackStages);
+    if (!mbar_wait(bar0 + 8u * st, static_cast<uint32_t>((j / kPackStages) & 1), abort_flag)) return false;
+    bulk_store(pdst[st], stage0 + st * kPackStage, pbytes[st]);
+    bulk_commit();
+    return true;
+  };
   const long long n_tiles = tiles_per_plane * n_planes;
-  for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+  for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
     const int plane = static_cast<int>(tile / tiles_per_plane);
-    const long long t0 = (tile - plane * tiles_per_plane) * kPackTile;
-    int r = find_run(runs, n_runs, t0);              // same address on every thread: a broadcast load
-    long long next = r + 1 < n_runs ? __ldg(&runs[r + 1].vec0) : total_vecs;
-    uint4 val[kPackUnroll];
-    uint4* dst[kPackUnroll];
-#pragma unroll
-    for (int u = 0; u < kPackUnroll; ++u) {
-      const long long v = t0 + threadIdx.x + u * kPackThreads;
-      dst[u] = nullptr;
-      if (v < total_vecs) {
-        while (v >= next) {                          // the thread's run moves forward only
-          ++r;
-          next = r + 1 < n_runs ? __ldg(&runs[r + 1].vec0) : total_vecs;
-        }
-        const long long off = (v - __ldg(&runs[r].vec0)) * 16;
-        const int ss = __ldg(&runs[r].src_slot), ds = __ldg(&runs[r].dst_slot);
-        const uint4* src =
-            reinterpret_cast<const uint4*>(bases.src[plane * n_slots + ss] + __ldg(&runs[r].src_off) + off);
-        dst[u] = reinterpret_cast<uint4*>(bases.dst[plane * n_slots + ds] + __ldg(&runs[r].dst_off) + off);
-        val[u] = __ldcs(src);                        // source rows are read once: streaming load
+    long long b = (tile - plane * tiles_per_plane) * kPackTile;
+    const long long e = b + kPackTile < total_bytes ? b + kPackTile : total_bytes;
+    int r = find_run(runs, n_runs, b >> 4);
+    while (ok && b < e) {
+      const long long r0 = __ldg(&runs[r].vec0) << 4;
+      const long long r1 = r + 1 < n_runs ? __ldg(&runs[r + 1].vec0) << 4 : total_bytes;
+      if (b >= r1) {                                   // past this run (or an empty one): the next
+        ++r;
+        continue;
       }
+      long long pe = b + kPackStage;
+      if (pe > r1) pe = r1;
+      if (pe > e) pe = e;
+      const int st = static_cast<int>(issued % kPackStages);
+      if (issued >= kPackStages) bulk_wait_read<kPackStages - kPackLag - 1>();   // store of piece issued - S read
+      const int ss = __ldg(&runs[r].src_slot), ds = __ldg(&runs[r].dst_slot);
+      const uint8_t* src = bases.src[plane * n_slots + ss] + __ldg(&runs[r].src_off) + (b - r0);
+      pdst[st] = bases.dst[plane * n_slots + ds] + __ldg(&runs[r].dst_off) + (b - r0);
+      pbytes[st] = static_cast<uint32_t>(pe - b);
+      mbar_expect_tx(bar0 + 8u * st, pbytes[st]);
+      bulk_load(stage0 + st * kPackStage, src, pbytes[st], bar0 + 8u * st, pol);
+      ++issued;
+      if (issued > kPackLag) {
+        ok = store(stored);
+        stored += ok;
+      }
+      b = pe;
     }
-#pragma unroll
-    for (int u = 0; u < kPackUnroll; ++u)
-      if (dst[u] != nullptr) *dst[u] = val[u];
   }
+  while (ok && stored < issued) {
+    ok = store(stored);
+    stored += ok;
+  }
+  if (!ok) {
+    // wind down: the loads still in flight must land before the CTA's shared memory is released
+    for (long long j = stored; j < issued; ++j) {
+      const int st = static_cast<int>(j % kPackStages);
+      const unsigned long long t0 = global_ns();
+      while (!mbar_try_wait(bar0 + 8u * st, static_cast<uint32_t>((j / kPackStages) & 1)))
+        if (global_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (err != nullptr) atomicOr(err, kErrTimeoutPack);
+  }
+  bulk_wait<0>();
 }
 
 // Merge weights of two partial results by their log-sum-exp (m = max(l1, l2), 0 when both are -inf):
@@ -192,7 +234,7 @@ extern "C" long long orl_pack_prepare(orl_copy_run* runs, const int64_t* nbytes,
 
 extern "C" int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_vecs, int n_planes, int n_slots,
                         const void* const* src_bases, void* const* dst_bases, const int32_t* seg_len_dev, int n_seg,
-                        int32_t* cu_out_dev, void* stream_ptr) {
+                        int32_t* cu_out_dev, int* err_dev, void* stream_ptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (n_planes < 1 || n_planes > kMaxPlanes || n_slots < 1 || n_slots > kMaxSlots || n_runs < 0 || total_vecs < 0)
     return ORL_ERR_ARG;
@@ -206,18 +248,24 @@ extern "C" int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long tota
     b.dst[i] = static_cast<uint8_t*>(dst_bases ? dst_bases[i] : nullptr);
     if ((reinterpret_cast<uintptr_t>(b.src[i]) | reinterpret_cast<uintptr_t>(b.dst[i])) & 15u) return ORL_ERR_ALIGN;
   }
-  int dev = 0, sms = 148, per_sm = 4;
+  int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pack_kernel, kPackThreads, 0);
-  const long long tiles_per_plane = (total_vecs + kPackTile - 1) / kPackTile;
+  static bool smem_set[64] = {};                     // the shared-memory opt-in, once per device
+  if (dev < 0 || dev >= 64) return ORL_ERR_LAUNCH;
+  if (!smem_set[dev]) {
+    if (cudaFuncSetAttribute(pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmem) != cudaSuccess)
+      return ORL_ERR_LAUNCH;
+    smem_set[dev] = true;
+  }
+  const long long total_bytes = total_vecs * 16;
+  const long long tiles_per_plane = (total_bytes + kPackTile - 1) / kPackTile;
   long long blocks = tiles_per_plane * n_planes;
-  const long long cap = static_cast<long long>(sms) * (per_sm > 0 ? per_sm : 1);   // one resident wave
-  if (blocks > cap) blocks = cap;
+  if (blocks > sms) blocks = sms;                    // one CTA per SM: its shared memory is the copy ring
   if (blocks < 1) blocks = 1;
-  pack_kernel<<<static_cast<int>(blocks), kPackThreads, 0, stream>>>(runs_dev, n_runs, total_vecs, tiles_per_plane,
-                                                                     n_planes, n_slots, b, seg_len_dev, n_seg,
-                                                                     cu_out_dev);
+  pack_kernel<<<static_cast<int>(blocks), 32, kPackSmem, stream>>>(runs_dev, n_runs, total_bytes, tiles_per_plane,
+                                                                   n_planes, n_slots, b, seg_len_dev, n_seg,
+                                                                   cu_out_dev, err_dev);
   return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
 }
 

@@ -20,6 +20,7 @@ enum ErrorBits : int {
   kErrTimeoutMma = 2,       // MMA warp gave up waiting for a load or for P
   kErrTimeoutSoftmax = 4,   // softmax warps gave up waiting for S or O
   kErrTimeoutDrain = 8,     // wind-down gave up waiting for in-flight copies
+  kErrTimeoutPack = 16,     // pack kernel gave up waiting for a bulk load
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -94,6 +95,31 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(cache_hint)
       : "memory");
+}
+
+// Untiled bulk copies (the TMA engine moving a contiguous byte range; both addresses 16-byte aligned, size a multiple
+// of 16, no multicast). Load: global -> this CTA's shared memory, completing `bytes` of transaction on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                          uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(cache_hint)
+      : "memory");
+}
+// Store: shared -> global, tracked by bulk groups (bulk_commit closes a group; bulk_wait_read<N> returns once at most
+// N groups still read shared memory, bulk_wait<N> once at most N are incomplete).
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // L2 eviction-priority policies for cache_hint operands.

@@ -7,9 +7,12 @@
 //     diffusers' apply_rotary_emb over interleaved pairs (cos / sin repeated per pair).
 // Both rotations are out[2i] = x[2i] c_i - x[2i+1] s_i, out[2i+1] = x[2i] s_i + x[2i+1] c_i with c_i = cos[row][2i]
 // and s_i = sin[row][2i + sin_shift] (sin_shift 0 for the repeated tables, 1 for Wan's).
-// One warp per (row, group): a group is one head (per-head norm) or the whole row (hidden norm); each lane holds
-// 8-element chunks (16-byte loads), the sum of squares is reduced with warp shuffles in fp32, and the output is
-// written to out_row_map[row] (or row) — i.e. straight into a packed layout when a row map is given.
+// One block per kRowsPerBlock rows, one thread per 8 consecutive elements of each (16-byte loads and stores; all of a
+// thread's loads — its x vectors, cos / sin entries and weights — issued before any reduction, for memory-level
+// parallelism): the sum of squares is reduced over the group's threads (per-head norm: the head_dim / 8 consecutive
+// lanes of a head, by shuffles; hidden norm: the whole block, shuffles then shared memory), in fp32. A thread's cos /
+// sin entries are table columns d .. d + 7 of its head position d; the output goes to row_map[row] (or row) —
+// straight into a packed layout when a row map is given.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -19,65 +22,106 @@
 
 namespace orl {
 
-template <int kChunksPerLane>
-__global__ void qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
-                                    const __nv_bfloat16* __restrict__ weight, const float* __restrict__ cos_t,
-                                    const float* __restrict__ sin_t, long long rows, int heads, int head_dim,
-                                    int per_head, float eps, int sin_shift, long long rope_ld,
-                                    const int32_t* __restrict__ row_map, long long n_groups_per_row) {
-  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const long long row = warp_id / n_groups_per_row;
-  if (row >= rows) return;
-  const int group = static_cast<int>(warp_id - row * n_groups_per_row);
-  const int hidden = heads * head_dim;
-  const int glen = per_head ? head_dim : hidden;        // elements normalised together
-  const int gbase = group * glen;                        // first element of the group in the row
-  const __nv_bfloat16* xr = x + row * hidden + gbase;
-  float v[kChunksPerLane][8];
-  float ss = 0.f;
+constexpr int kRowsPerBlock = 2;
+
+__global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           __nv_bfloat16* __restrict__ y,
+                                                           const __nv_bfloat16* __restrict__ weight,
+                                                           const float* __restrict__ cos_t,
+                                                           const float* __restrict__ sin_t, long long rows,
+                                                           int hidden, int head_dim, int per_head, float eps,
+                                                           int sin_shift, long long rope_ld,
+                                                           const int32_t* __restrict__ row_map) {
+  __shared__ float part[kRowsPerBlock][32];
+  const int t = threadIdx.x;
+  const int e = 8 * t;                                   // first element of this thread in a row
+  const bool active = e < hidden;
+  const int d = active ? e % head_dim : 0;               // position within the head (8 elements never straddle heads)
+  const long long row0 = static_cast<long long>(blockIdx.x) * kRowsPerBlock;
+  uint4 raw[kRowsPerBlock];
+  float4 c[kRowsPerBlock][2], sn4[kRowsPerBlock][2];
+  uint4 wr = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-  for (int c = 0; c < kChunksPerLane; ++c) {
-    const int e = (c * 32 + lane) * 8;
-    if (e < glen) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(xr + e);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h2[i]);
-        v[c][2 * i] = f.x;
-        v[c][2 * i + 1] = f.y;
-        ss += f.x * f.x + f.y * f.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
-    }
+  for (int k = 0; k < kRowsPerBlock; ++k) {
+    const long long row = row0 + k;
+    raw[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (active && row < rows) raw[k] = __ldcs(reinterpret_cast<const uint4*>(x + row * hidden + e));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / glen + eps);
-  const long long orow = row_map ? row_map[row] : row;
-  __nv_bfloat16* yr = y + orow * hidden + gbase;
-  const float* cr = cos_t + row * rope_ld;
-  const float* sr = sin_t + row * rope_ld;
+  for (int k = 0; k < kRowsPerBlock; ++k) {
+    const long long row = row0 + k;
+    if (active && row < rows) {
+      const float4* cr = reinterpret_cast<const float4*>(cos_t + row * rope_ld + d);
+      const float4* sr = reinterpret_cast<const float4*>(sin_t + row * rope_ld + d);
+      c[k][0] = __ldg(cr);
+      c[k][1] = __ldg(cr + 1);
+      sn4[k][0] = __ldg(sr);
+      sn4[k][1] = __ldg(sr + 1);
+    }
+  }
+  if (active) wr = __ldg(reinterpret_cast<const uint4*>(weight + (per_head ? d : e)));
+  float v[kRowsPerBlock][8], ss[kRowsPerBlock];
 #pragma unroll
-  for (int c = 0; c < kChunksPerLane; ++c) {
-    const int e = (c * 32 + lane) * 8;
-    if (e >= glen) continue;
-    uint4 packed;
-    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+  for (int k = 0; k < kRowsPerBlock; ++k) {
+    const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+    ss[k] = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int g = gbase + e + 2 * i;                   // element index in the row
-      const int d = g % head_dim;                        // position within the head (pairs never straddle heads)
-      const float w0 = __bfloat162float(weight[per_head ? d : g]);
-      const float w1 = __bfloat162float(weight[per_head ? d + 1 : g + 1]);
-      const float a = v[c][2 * i] * inv * w0, b = v[c][2 * i + 1] * inv * w1;
-      const float cs = cr[d], sn = sr[d + sin_shift];
-      o2[i] = __floats2bfloat162_rn(a * cs - b * sn, a * sn + b * cs);
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      v[k][2 * i] = f.x;
+      v[k][2 * i + 1] = f.y;
+      ss[k] += f.x * f.x + f.y * f.y;
     }
-    *reinterpret_cast<uint4*>(yr + e) = packed;
+  }
+  float inv[kRowsPerBlock];
+  if (per_head) {
+    // head_dim / 8 lanes per head (a power of two <= 32, heads aligned to those lane groups)
+#pragma unroll
+    for (int k = 0; k < kRowsPerBlock; ++k) {
+      for (int o = (head_dim >> 4); o > 0; o >>= 1) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], o);
+      inv[k] = rsqrtf(ss[k] / head_dim + eps);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kRowsPerBlock; ++k) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], o);
+      if ((t & 31) == 0) part[k][t >> 5] = ss[k];
+    }
+    __syncthreads();
+    if (t < 32) {
+#pragma unroll
+      for (int k = 0; k < kRowsPerBlock; ++k) {
+        float a = t < static_cast<int>(blockDim.x >> 5) ? part[k][t] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (t == 0) part[k][0] = a;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kRowsPerBlock; ++k) inv[k] = rsqrtf(part[k][0] / hidden + eps);
+  }
+  if (!active) return;
+  const uint32_t ww[4] = {wr.x, wr.y, wr.z, wr.w};
+#pragma unroll
+  for (int k = 0; k < kRowsPerBlock; ++k) {
+    const long long row = row0 + k;
+    if (row >= rows) break;
+    const float cs[4] = {c[k][0].x, c[k][0].z, c[k][1].x, c[k][1].z};
+    const float sn[4] = {sin_shift ? sn4[k][0].y : sn4[k][0].x, sin_shift ? sn4[k][0].w : sn4[k][0].z,
+                         sin_shift ? sn4[k][1].y : sn4[k][1].x, sin_shift ? sn4[k][1].w : sn4[k][1].z};
+    uint4 packed;
+    uint32_t* o = &packed.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 wf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
+      const float a = v[k][2 * i] * inv[k] * wf.x, b = v[k][2 * i + 1] * inv[k] * wf.y;
+      const __nv_bfloat162 r = __floats2bfloat162_rn(a * cs[i] - b * sn[i], a * sn[i] + b * cs[i]);
+      o[i] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    const long long orow = row_map ? row_map[row] : row;
+    *reinterpret_cast<uint4*>(y + orow * hidden + e) = packed;
   }
 }
 
@@ -119,26 +163,21 @@ extern "C" int orl_qk_norm_rope(const void* x, void* y, const void* weight, cons
   if (rows < 0 || heads <= 0 || head_dim <= 0 || (head_dim & 7) || sin_shift < 0 || sin_shift > 1 || rope_ld < head_dim)
     return ORL_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) return ORL_ERR_ALIGN;
+  const int hidden = heads * head_dim;
+  // per-head norm: head_dim / 8 lanes per head must be a power of two within a warp; one thread per 8 elements
+  if (per_head && ((head_dim >> 3) > 32 || ((head_dim >> 3) & ((head_dim >> 3) - 1)) != 0)) return ORL_ERR_UNSUPPORTED;
+  if (hidden / 8 > 1024) return ORL_ERR_UNSUPPORTED;
+  // 16-byte vectors of the tables and the weight
+  if ((rope_ld & 3) || ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t) |
+                         reinterpret_cast<uintptr_t>(weight)) & 15u))
+    return ORL_ERR_ALIGN;
   if (rows == 0) return ORL_OK;
-  const int glen = per_head ? head_dim : heads * head_dim;
-  const int chunks = (glen / 8 + 31) / 32;
-  const long long groups = per_head ? heads : 1;
-  const long long warps = rows * groups;
-  const int threads = 256;
-  const long long blocks = (warps * 32 + threads - 1) / threads;
+  const long long blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
   if (blocks > 0x7fffffffLL) return ORL_ERR_ARG;
-#define ORL_QKNR(N)                                                                                               \
-  qk_norm_rope_kernel<N><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(                                 \
-      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y),                                       \
-      static_cast<const __nv_bfloat16*>(weight), cos_t, sin_t, rows, heads, head_dim, per_head, eps, sin_shift,   \
-      rope_ld, row_map, groups)
-  if (chunks <= 1) ORL_QKNR(1);
-  else if (chunks <= 2) ORL_QKNR(2);
-  else if (chunks <= 4) ORL_QKNR(4);
-  else if (chunks <= 8) ORL_QKNR(8);
-  else if (chunks <= 16) ORL_QKNR(16);
-  else return ORL_ERR_UNSUPPORTED;
-#undef ORL_QKNR
+  const int threads = ((hidden / 8 + 31) / 32) * 32;
+  qk_norm_rope_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(weight),
+      cos_t, sin_t, rows, hidden, head_dim, per_head, eps, sin_shift, rope_ld, row_map);
   return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
 }
 

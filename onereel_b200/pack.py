@@ -14,6 +14,12 @@ import torch
 from onereel_b200 import _lib as L
 
 
+def _err_word(device):
+    # the error word the attention launches on this device report through (attention.check reads it)
+    from onereel_b200.attention import _err_word as word
+    return word(device)
+
+
 class RunTable:
     """a prepared run table on one device: runs_dev (uint8 view of orl_copy_run [n]), total 16-byte vectors"""
     launches = 0          # pack launches issued by this process (benchmark launch accounting)
@@ -42,7 +48,8 @@ class RunTable:
         L.check(L.lib().orl_pack(self.dev.data_ptr() if self.dev is not None else None, self.n_runs, self.total_vecs,
                                  n_planes, n_slots, SrcArr(*src_bases), SrcArr(*dst_bases),
                                  None if seg_len_dev is None else seg_len_dev.data_ptr(), n_seg,
-                                 None if cu_out is None else cu_out.data_ptr(), s), 'orl_pack')
+                                 None if cu_out is None else cu_out.data_ptr(), _err_word(self.device).data_ptr(),
+                                 s), 'orl_pack')
 
 
 def row_bytes(x: torch.Tensor) -> int:
