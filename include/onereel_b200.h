@@ -87,6 +87,20 @@ ORL_API int orl_attn_fwd(const void* q, const void* k, const void* v, void* out,
                  int heads, int head_dim, float scale, const orl_attn_work* work_dev, int n_items, int* err_dev,
                  void* stream);
 
+/* The varlen call with cu_seqlens in DEVICE memory, as the reference passes them to FlashAttention
+ * (attention.py:28-29 `cu_seqlens`, 39-43 `varlen`): cu_q_dev / cu_k_dev int32 [n_seg + 1] on the device. The work
+ * list is planned on the device (same items and order as orl_attn_plan), so the call returns without waiting for the
+ * GPU. work_dev: caller scratch of work_capacity items, at least orl_attn_fwd_cu_capacity(nq, n_seg, heads) (slot 0
+ * receives the planned item count). cu_seqlens that decrease or leave [0, nq] / [0, nk] compute nothing and set an
+ * error bit in err_dev (orl_error_bits_describe). At most 4096 segments. head_dim 64 or 128. */
+ORL_API int orl_attn_fwd_cu(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
+                            long long nk, int heads, int head_dim, float scale, const int32_t* cu_q_dev,
+                            const int32_t* cu_k_dev, int n_seg, orl_attn_work* work_dev, long long work_capacity,
+                            int* err_dev, void* stream);
+
+/* Work-list slots orl_attn_fwd_cu needs: 1 + heads * (ceil(nq / 256) + n_seg). */
+ORL_API long long orl_attn_fwd_cu_capacity(long long nq, int n_seg, int heads);
+
 /* Allocation-free variant of orl_attn_fwd, for callers that cannot call cudaMalloc (code inside another
  * framework's memory pool or allocator hook, or a plugin host that owns all device memory) and so cannot supply the
  * work list and error word orl_attn_fwd needs. Has no counterpart in the reference. The scratch lives in a

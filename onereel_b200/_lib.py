@@ -61,6 +61,9 @@ SIGNATURES = {
     'orl_attn_plan_ranges': (c_int, [P_I32, P_I32, P_I32, P_I32, c_int, c_int, c_vp, c_int]),
     'orl_attn_fwd': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_int, c_int, c_float, c_vp, c_int, c_vp,
                              c_vp]),
+    'orl_attn_fwd_cu': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_int, c_int, c_float, c_vp, c_vp, c_int,
+                                c_vp, c_ll, c_vp, c_vp]),
+    'orl_attn_fwd_cu_capacity': (c_ll, [c_ll, c_int, c_int]),
     'orl_attn_fwd_noalloc': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_int, c_int, c_float, P_I32, P_I32,
                                      c_int, c_vp, c_vp]),
     'orl_pack_prepare': (c_ll, [c_vp, P_I64, c_int]),

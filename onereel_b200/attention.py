@@ -48,14 +48,15 @@ def _err_word(device: torch.device) -> torch.Tensor:
 
 
 def check(device=None) -> None:
-    """synchronise and raise if a kernel on `device` (default: every device used) reported a timeout"""
+    """synchronise and raise if a kernel on `device` (default: every device used) set a bit in its error word (a
+    bounded wait that ran out, or cu_seqlens the device planner rejected)"""
     for key, w in list(_ERR.items()):
         if device is not None and torch.device(device).index not in (None, key):
             continue
         bits = int(w.item())
         if bits:
             w.zero_()
-            raise L.OrlError(f'attention kernel on cuda:{key} gave up waiting: {L.describe_error_bits(bits)}')
+            raise L.OrlError(f'kernel on cuda:{key} reported: {L.describe_error_bits(bits)}')
 
 
 def plan(q_start, q_len, k_start, k_len, heads: int, device) -> tuple[torch.Tensor, int]:
@@ -146,13 +147,50 @@ def _cu_to_ranges(cu_q, cu_k):
     return qs, ql, ks, kl
 
 
+_CU_WORK = {}    # (device, stream) -> work-list scratch of orl_attn_fwd_cu (uint8), grown as needed
+
+
+def _attend_cu(q, k, v, cu_q, cu_k, lse):
+    """cu_seqlens on the device: orl_attn_fwd_cu plans the work list on the GPU, no host synchronisation. The
+    scratch is per (device, stream), so calls on one stream reuse it in order."""
+    _check_inputs(q, k, v)
+    for name, c in (('cu_seqlens_q', cu_q), ('cu_seqlens_k', cu_k)):
+        if c.dtype != torch.int32 or c.dim() != 1 or c.device != q.device or not c.is_contiguous():
+            raise TypeError(f'{name} must be a contiguous int32 tensor on {q.device}')
+    if cu_q.numel() != cu_k.numel() or cu_q.numel() < 1:
+        raise ValueError('cu_seqlens_q and cu_seqlens_k differ in length')
+    Nq, H, Dh = q.shape
+    dev = q.device
+    n_seg = cu_q.numel() - 1
+    need = L.check(L.lib().orl_attn_fwd_cu_capacity(Nq, n_seg, H), 'orl_attn_fwd_cu_capacity')
+    stream = torch.cuda.current_stream(dev)
+    key = (dev.index, stream.cuda_stream)
+    work = _CU_WORK.get(key)
+    if work is None or work.numel() < need * L.WORK_DTYPE.itemsize:
+        work = _CU_WORK[key] = torch.empty(need * L.WORK_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+    out = torch.empty_like(q)
+    lse_t = torch.empty(H, Nq, dtype=torch.float32, device=dev) if lse else None
+    L.check(L.lib().orl_attn_fwd_cu(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                    None if lse_t is None else lse_t.data_ptr(), Nq, k.shape[0], H, Dh, Dh ** -0.5,
+                                    cu_q.data_ptr(), cu_k.data_ptr(), n_seg, work.data_ptr(),
+                                    work.numel() // L.WORK_DTYPE.itemsize, _err_word(dev).data_ptr(),
+                                    stream.cuda_stream), 'orl_attn_fwd_cu')
+    return out, lse_t
+
+
 def varlen(q, k, v, cu_q, cu_k, max_q, max_k):
-    """attention.py:39-43: packed q [Nq, H, D], k / v [Nk, H, D] -> out [Nq, H, D]"""
+    """attention.py:39-43: packed q [Nq, H, D], k / v [Nk, H, D] -> out [Nq, H, D]. cu_seqlens as device int32
+    tensors (as the reference passes them) are planned on the GPU without a host sync; host lists are planned on
+    the host."""
+    if isinstance(cu_q, torch.Tensor) and cu_q.is_cuda:
+        return _attend_cu(q, k, v, cu_q, cu_k, lse=False)[0]
     return attend(q, k, v, *_cu_to_ranges(cu_q, cu_k))[0]
 
 
 def varlen_lse(q, k, v, cu_q, cu_k, max_q, max_k):
     """attention.py:46-53: (out [Nq, H, D], lse [H, Nq] fp32, natural log)"""
+    if isinstance(cu_q, torch.Tensor) and cu_q.is_cuda:
+        return _attend_cu(q, k, v, cu_q, cu_k, lse=True)
     return attend(q, k, v, *_cu_to_ranges(cu_q, cu_k), lse=True)
 
 

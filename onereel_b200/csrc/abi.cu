@@ -32,6 +32,7 @@ extern "C" int orl_error_bits_describe(int bits, char* buf, int cap) {
       {orl::kErrTimeoutSoftmax, "softmax warps timed out waiting for S or O"},
       {orl::kErrTimeoutDrain, "wind-down timed out waiting for in-flight copies"},
       {orl::kErrTimeoutPack, "pack kernel timed out waiting for a bulk copy"},
+      {orl::kErrPlan, "cu_seqlens rejected on the device (decreasing or outside the tensors): nothing computed"},
   };
   int n = 0;
   for (const auto& e : names)

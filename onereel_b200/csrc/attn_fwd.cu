@@ -60,6 +60,7 @@ struct AttnCfg {
 };
 
 constexpr int kThreads = 384;
+constexpr int kMaxDevices = 64;
 // register split: the launch has 384 threads x 168 registers; warpgroup 0 (producer, MMA issuer, two idle warps)
 // keeps kRegsLow, the two softmax warpgroups get kRegsHigh (4 x 32 x kRegsLow + 8 x 32 x kRegsHigh = 384 x 168)
 constexpr int kLaunchRegs = 168, kRegsLow = 120, kRegsHigh = 192;
@@ -412,8 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnWork* __restrict__ work,
                     __nv_bfloat16* __restrict__ out, float* __restrict__ lse, long long nq_total, int heads,
-                    float scale_log2, int* __restrict__ err) {
+                    float scale_log2, int* __restrict__ err, const int* __restrict__ n_items_dev) {
   using C = AttnCfg<D>;
+  // a grid sized by an upper bound (work list planned on the device): CTAs past the planned count have no item
+  if (n_items_dev != nullptr && static_cast<int>(blockIdx.x) >= __ldg(n_items_dev)) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOff + C::kNumBars * 8);
@@ -509,29 +512,37 @@ static int make_rows_map(CUtensorMap* map, const void* base, long long rows, int
 template <int D>
 static int launch_attn(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
                        long long nk, int heads, float scale, const AttnWork* work, int n_items, int* err,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const int* n_items_dev = nullptr) {
   using C = AttnCfg<D>;
   CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_rows_map(&mq, q, nq, heads * D)) != ORL_OK) return rc;
   if ((rc = make_rows_map(&mk, k, nk, heads * D)) != ORL_OK) return rc;
   if ((rc = make_rows_map(&mv, v, nk, heads * D)) != ORL_OK) return rc;
-  static std::once_flag once;
-  static cudaError_t attr_rc = cudaSuccess;
+  // the shared-memory opt-in is a per-device attribute: set once for every device the kernel runs on
+  static std::mutex mu;
+  static bool attr_set[kMaxDevices] = {};
   static int launch_regs = 0;
-  std::call_once(once, [] {
-    attr_rc = cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    cudaFuncAttributes fa{};
-    if (attr_rc == cudaSuccess) attr_rc = cudaFuncGetAttributes(&fa, attn_fwd_kernel<D>);
-    launch_regs = fa.numRegs;
-  });
-  if (attr_rc != cudaSuccess) return ORL_ERR_LAUNCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ORL_ERR_LAUNCH;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      if (cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+          cudaSuccess)
+        return ORL_ERR_LAUNCH;
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, attn_fwd_kernel<D>) != cudaSuccess) return ORL_ERR_LAUNCH;
+      launch_regs = fa.numRegs;
+      attr_set[dev] = true;
+    }
+  }
   // the setmaxnreg split assumes exactly kLaunchRegs registers per thread at launch; any other count could leave
   // the increasing warpgroups waiting for registers that were never freed, so such a build is never launched
   if (launch_regs != kLaunchRegs) return ORL_ERR_UNSUPPORTED;
   const float scale_log2 = scale * 1.4426950408889634f;
   attn_fwd_kernel<D><<<n_items, kThreads, C::kSmemBytes, stream>>>(
-      mq, mk, mv, work, static_cast<__nv_bfloat16*>(out), lse, nq, heads, scale_log2, err);
+      mq, mk, mv, work, static_cast<__nv_bfloat16*>(out), lse, nq, heads, scale_log2, err, n_items_dev);
   return cudaGetLastError() == cudaSuccess ? ORL_OK : ORL_ERR_LAUNCH;
 }
 
@@ -610,6 +621,158 @@ extern "C" int orl_attn_fwd(const void* q, const void* k, const void* v, void* o
   }
 }
 
+// ------------------------------------------------------------------------------------------------ device plan
+// orl_attn_fwd_cu: the varlen call with cu_seqlens already on the device (the reference hands FlashAttention device
+// tensors, attention.py:28-29, 39-43) — the work list is planned on the device, so the call never waits for the GPU.
+// One block reads cu_q / cu_k, checks them (non-decreasing, inside [0, nq] / [0, nk]), orders the segments with query
+// rows by key count, descending and stable — the order orl_attn_plan_ranges uses, so the items and the results are
+// identical — and writes the item count into slot 0 of the work buffer and the items after it. The attention grid is
+// sized by the upper bound heads x (ceil(nq / 256) + n_seg); CTAs past the planned count return at once.
+namespace orl {
+
+constexpr int kDevPlanMaxSeg = 4096;
+
+__global__ void __launch_bounds__(1024) plan_device_kernel(const int32_t* __restrict__ cu_q,
+                                                           const int32_t* __restrict__ cu_k, int n_seg, int heads,
+                                                           long long nq, long long nk, AttnWork* __restrict__ work,
+                                                           long long capacity, int* __restrict__ err) {
+  extern __shared__ int plan_smem[];
+  int* s_lq = plan_smem;                    // [n_seg] query rows
+  int* s_lk = s_lq + n_seg;                 // [n_seg] key rows
+  int* s_seg = s_lk + n_seg;                // [n_seg] segment at each rank (ranks of segments with query rows)
+  int* s_end = s_seg + n_seg;               // [n_seg] end of each rank's items (inclusive scan in rank order)
+  __shared__ int bad, n_ranked, total;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    bad = 0;
+    n_ranked = 0;
+    total = 0;
+  }
+  __syncthreads();
+  for (int i = t; i < n_seg; i += blockDim.x) {
+    const long long q0 = cu_q[i], q1 = cu_q[i + 1], k0 = cu_k[i], k1 = cu_k[i + 1];
+    if (q0 < 0 || q1 < q0 || q1 > nq || k0 < 0 || k1 < k0 || k1 > nk) bad = 1;
+    s_lq[i] = static_cast<int>(q1 - q0);
+    s_lk[i] = static_cast<int>(k1 - k0);
+  }
+  __syncthreads();
+  if (bad) {
+    if (t == 0) {
+      work[0].q_row0 = 0;
+      atomicOr(err, kErrPlan);
+    }
+    return;
+  }
+  // rank of segment i among the segments with query rows: more keys first, then the lower index; its items start
+  // after those of every segment ranked before it
+  for (int i = t; i < n_seg; i += blockDim.x) {
+    const int lq = s_lq[i], lk = s_lk[i];
+    if (lq == 0) continue;
+    int rank = 0;
+    long long before = 0;
+    for (int j = 0; j < n_seg; ++j) {
+      const int lqj = s_lq[j], lkj = s_lk[j];
+      if (lqj > 0 && (lkj > lk || (lkj == lk && j < i))) {
+        ++rank;
+        before += static_cast<long long>(heads) * ((lqj + 255) >> 8);
+      }
+    }
+    const long long cnt = static_cast<long long>(heads) * ((lq + 255) >> 8);
+    s_seg[rank] = i;
+    s_end[rank] = static_cast<int>(before + cnt);
+    atomicAdd(&n_ranked, 1);
+    atomicAdd(&total, static_cast<int>(cnt));
+  }
+  __syncthreads();
+  const int n = total, m = n_ranked;
+  if (static_cast<long long>(n) + 1 > capacity) {
+    if (t == 0) {
+      work[0].q_row0 = 0;
+      atomicOr(err, kErrPlan);
+    }
+    return;
+  }
+  for (int it = t; it < n; it += blockDim.x) {
+    int lo = 0, hi = m - 1;                 // first rank whose items end after it
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (s_end[mid] > it) hi = mid; else lo = mid + 1;
+    }
+    const int i = s_seg[lo];
+    const int lq = s_lq[i];
+    const int chunks = (lq + 255) >> 8;
+    const int r = it - (lo > 0 ? s_end[lo - 1] : 0);
+    const int h = r / chunks, c = r - h * chunks;
+    AttnWork w;
+    w.q_row0 = cu_q[i] + 256 * c;
+    w.q_len = min(256, lq - 256 * c);
+    w.k_row0 = cu_k[i];
+    w.k_len = s_lk[i];
+    w.head = h;
+    w.seg = i;
+    w.pad0 = w.pad1 = 0;
+    work[1 + it] = w;
+  }
+  if (t == 0) work[0].q_row0 = n;
+}
+
+}  // namespace orl
+
+extern "C" long long orl_attn_fwd_cu_capacity(long long nq, int n_seg, int heads) {
+  if (nq < 0 || n_seg < 0 || heads <= 0) return ORL_ERR_ARG;
+  return 1 + static_cast<long long>(heads) * ((nq + 255) / 256 + n_seg);
+}
+
+extern "C" int orl_attn_fwd_cu(const void* q, const void* k, const void* v, void* out, float* lse, long long nq,
+                               long long nk, int heads, int head_dim, float scale, const int32_t* cu_q_dev,
+                               const int32_t* cu_k_dev, int n_seg, orl_attn_work* work_dev, long long work_capacity,
+                               int* err_dev, void* stream_ptr) {
+  using namespace orl;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || cu_q_dev == nullptr || cu_k_dev == nullptr ||
+      work_dev == nullptr || err_dev == nullptr)
+    return ORL_ERR_ARG;
+  if (nq < 0 || nk < 0 || heads <= 0 || n_seg < 0 || !(scale > 0.f)) return ORL_ERR_ARG;
+  if (head_dim != 64 && head_dim != 128) return ORL_ERR_UNSUPPORTED;
+  if (n_seg > kDevPlanMaxSeg) return ORL_ERR_CAPACITY;
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+        reinterpret_cast<uintptr_t>(out)) & 15u) != 0)
+    return ORL_ERR_ALIGN;
+  const long long bound = orl_attn_fwd_cu_capacity(nq, n_seg, heads);
+  if (work_capacity < bound) return ORL_ERR_CAPACITY;
+  if (bound - 1 > 0x7fffffffLL) return ORL_ERR_ARG;
+  if (n_seg == 0 || nq == 0) return ORL_OK;
+  const int smem = 16 * n_seg;
+  static std::mutex mu;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ORL_ERR_LAUNCH;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      if (cudaFuncSetAttribute(plan_device_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               16 * kDevPlanMaxSeg) != cudaSuccess)
+        return ORL_ERR_LAUNCH;
+      attr_set[dev] = true;
+    }
+  }
+  plan_device_kernel<<<1, 1024, smem, stream>>>(cu_q_dev, cu_k_dev, n_seg, heads, nq, nk, work_dev, work_capacity,
+                                                err_dev);
+  if (cudaGetLastError() != cudaSuccess) return ORL_ERR_LAUNCH;
+  const void* kk = k;
+  const void* vv = v;
+  long long nkk = nk;
+  if (nk == 0) {   // every item has k_len 0 and loads nothing; the K/V maps only need a valid address
+    kk = vv = q;
+    nkk = nq;
+  }
+  const int grid = static_cast<int>(bound - 1);
+  const int* count = reinterpret_cast<const int*>(work_dev);   // slot 0: the planned item count
+  return head_dim == 64
+             ? launch_attn<64>(q, kk, vv, out, lse, nq, nkk, heads, scale, work_dev + 1, grid, err_dev, stream, count)
+             : launch_attn<128>(q, kk, vv, out, lse, nq, nkk, heads, scale, work_dev + 1, grid, err_dev, stream, count);
+}
+
 // ------------------------------------------------------------------------------------------------ allocation-free
 // orl_attn_fwd_noalloc serves callers that cannot call cudaMalloc at all — code running where the CUDA allocator
 // is off limits (inside another framework's memory pool or a custom allocator hook, in a plugin host that owns
@@ -633,7 +796,7 @@ constexpr int kNoAllocMaxItems = 16384;
 constexpr int kNoAllocMaxSegments = 1024;
 constexpr int kNoAllocHeaderBytes = 256;   // error word at offset 0, work items from offset 256
 constexpr int kNoAllocScratchBytes = kNoAllocHeaderBytes + kNoAllocMaxItems * static_cast<int>(sizeof(AttnWork));
-constexpr int kNoAllocMaxDevices = 64;
+constexpr int kNoAllocMaxDevices = kMaxDevices;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

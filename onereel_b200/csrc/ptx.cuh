@@ -21,6 +21,7 @@ enum ErrorBits : int {
   kErrTimeoutSoftmax = 4,   // softmax warps gave up waiting for S or O
   kErrTimeoutDrain = 8,     // wind-down gave up waiting for in-flight copies
   kErrTimeoutPack = 16,     // pack kernel gave up waiting for a bulk load
+  kErrPlan = 32,            // the device planner rejected cu_seqlens (decreasing or out of range): nothing computed
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

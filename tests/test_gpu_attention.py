@@ -210,3 +210,32 @@ def test_ring_single_rank_matches_oracle():
     dt = np.abs(ot.float().cpu().numpy() - want_t)
     d = np.concatenate([dv.ravel(), dt.ravel()])
     assert d.max() < MAX_ABS and d.mean() < MEAN_ABS, (d.max(), d.mean())
+
+
+@pytest.mark.parametrize('Dh', [128, 64])
+def test_varlen_device_cu_seqlens_plan_on_gpu(Dh):
+    """varlen with cu_seqlens on the device (orl_attn_fwd_cu: work list planned on the GPU) gives the same bits as
+    the host-planned call, for segments with no query rows, no keys, ragged lengths and equal key counts (the stable
+    order), and rejects decreasing cu_seqlens through the error word"""
+    from onereel_b200 import _lib as L, attention as A
+    H = 3
+    lq = [0, 300, 1, 257, 128, 0, 45, 600]
+    lk = [10, 129, 0, 400, 129, 7, 2000, 129]
+    q = rand(sum(lq), H, Dh, seed=11)
+    k = rand(sum(lk), H, Dh, seed=12)
+    v = rand(sum(lk), H, Dh, seed=13)
+    cq = torch.tensor(np.cumsum([0] + lq), dtype=torch.int32, device='cuda')
+    ck = torch.tensor(np.cumsum([0] + lk), dtype=torch.int32, device='cuda')
+    qs, ks = np.cumsum([0] + lq)[:-1].tolist(), np.cumsum([0] + lk)[:-1].tolist()
+    want, wl = A.attend(q, k, v, qs, lq, ks, lk, lse=True)
+    for _ in range(2):                                  # the scratch is reused by the second call
+        o, l = A.varlen_lse(q, k, v, cq, ck, max(lq), max(lk))
+        torch.cuda.synchronize()
+        A.check()
+        assert torch.equal(o, want)
+        assert torch.equal(l, wl)
+    bad = torch.tensor([0, 300, 200, sum(lq)], dtype=torch.int32, device='cuda')
+    A.varlen(q, k, v, bad, ck[:4].contiguous(), 300, 400)
+    torch.cuda.synchronize()
+    with pytest.raises(L.OrlError, match='cu_seqlens rejected'):
+        A.check()
