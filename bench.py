@@ -7,7 +7,8 @@ frames, 1590 tokens per frame, 128 text tokens per scene, frame memory {0, 8, 14
 hunyuan15.Processor.scene: the gather/pack launch (K and V of every segment) plus the attention launches, inputs
 resident in HBM. Useful FLOPs per step = sum over segments of 4 * lq * lk * H * D (experiments/kernel_breakdown.py:101
 of the reference) = 7.187 TFLOP. At N GPUs the headline runs cfg2's scene set repeated N times (weak scaling: about one
-cfg2 per GPU, every scene reading the same four frame-memory frames, exchanged over NCCL).
+cfg2 per GPU, every scene reading the same four frame-memory frames, pulled from their owner over NVLink peer memory;
+--exchange nccl moves them by NCCL send/recv instead, as the reference does).
 
 Beside the headline, the same JSON line carries, at every N (all timed on the device, max over ranks):
   parity       the rank's outputs of the timed path against a one-GPU recompute of the same rows on the same rank
@@ -208,7 +209,7 @@ def reduce(vals, op='max', dtype=torch.float64):
 class LayerBench:
     """one scene-attention layer on this rank through hunyuan15.Processor (scene or Ulysses by the plan)"""
 
-    def __init__(self, cfg, mode, overlap, dev):
+    def __init__(self, cfg, mode, overlap, dev, exchange='peer'):
         from onereel_b200 import dist as D, hunyuan15 as HY
         self.cfg, self.dev = cfg, dev
         self.rank, self.world = D.rank(), D.world()
@@ -216,7 +217,7 @@ class LayerBench:
         self.T, self.H, self.Dh = cfg['T'], cfg['heads'], cfg['dim']
         self.counts = [cfg['text']] * lay.n_scenes
         self.ctx = HY.Context(lay, mode=mode, T=self.T, counts={True: self.counts, False: self.counts}, fwd=1,
-                              overlap=overlap)
+                              overlap=overlap, exchange=exchange)
         HY.plan_parallel(self.ctx, self.H)
         self.proc = HY.Processor(self.ctx, 0)
         self.own = tuple(self.ctx.own[self.rank])
@@ -344,8 +345,8 @@ class LayerBench:
         """device time per phase of the step on every rank (events on the compute stream; 'exchange_wait' = the time
         the compute stream stood waiting for the K/V exchange), mean over steps: a list indexed by rank"""
         from onereel_b200 import hunyuan15 as HY
-        names = ['near', 'far_local', 'exchange_wait', 'far', 'far_remote', 'text_sync', 'a2a_in', 'attention',
-                 'a2a_out']
+        names = ['exchange', 'near', 'far_local', 'exchange_wait', 'far', 'far_remote', 'text_sync', 'a2a_in',
+                 'attention', 'a2a_out']
         HY.PHASES = []
         for _ in range(steps):
             self.step()
@@ -377,14 +378,15 @@ class LayerBench:
             return None
         lay, T, own_all, r = self.lay, self.T, self.ctx.own, self.rank
         k, v = self.inputs[1], self.inputs[2]
+        kind = self.ctx.exchange
         for _ in range(3):
-            comm.HaloExchange(lay, own_all, T, k, v).wait()
+            comm.kv_exchange(kind, lay, own_all, T, k, v).wait()
         torch.cuda.synchronize()
         D.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(self.stream)
         for _ in range(steps):
-            comm.HaloExchange(lay, own_all, T, k, v).wait()
+            comm.kv_exchange(kind, lay, own_all, T, k, v).wait()
         e1.record(self.stream)
         torch.cuda.synchronize()
         D.barrier()
@@ -409,10 +411,19 @@ class LayerBench:
                 t_in += t1 - t0
         ms_max, = reduce([ms], 'max')
         b_in, b_out, tb_in, tb_out = reduce([rows_in * rb, rows_out * rb, t_in * rb // 2, t_out * rb // 2], 'max')
-        return dict(exchange=dict(ms_alone=ms_max, bytes_in_max=b_in, bytes_out_max=b_out,
-                                  broadcast_rows=bcast, note='grouped NCCL send/recv of K and V plus the broadcast of '
-                                  'rows every rank reads; bytes per GPU and direction, max over ranks (a broadcast '
-                                  'counted once at its root)'),
+        if kind == 'peer' and comm.PEER_UNAVAILABLE is None:
+            # every reader pulls from the owner: the owner's outgoing bytes count each reader
+            rows_out = sum(hi - lo for q in range(n) if q != r for lo, hi in comm.clip(need[q], *own_all[r]))
+            b_in, b_out = reduce([rows_in * rb, rows_out * rb], 'max')
+            note = ('K and V of this rank copied into its symmetric buffer, device barrier, every interval pulled '
+                    'from its owner over NVLink (one TMA bulk-copy launch); bytes per GPU and direction, max over '
+                    'ranks')
+        else:
+            kind = 'nccl'
+            note = ('grouped NCCL send/recv of K and V plus the broadcast of rows every rank reads; bytes per GPU '
+                    'and direction, max over ranks (a broadcast counted once at its root)')
+        return dict(exchange=dict(kind=kind, ms_alone=ms_max, bytes_in_max=b_in, bytes_out_max=b_out,
+                                  broadcast_rows=bcast, note=note),
                     text_rows=dict(bytes_in_max=tb_in, bytes_out_max=tb_out))
 
 
@@ -732,6 +743,9 @@ def main():
                     help="K/V gathering: 'lse' attends far scenes to their local keys while the exchange is in flight "
                          "and merges by log-sum-exp (Context.overlap of the reference); 'auto' takes 'lse' from 4 "
                          "GPUs up (measured on 8 B200: +8 %% on the weak cfg2 layer; on 2 the two are even)")
+    ap.add_argument('--exchange', default='peer', choices=['peer', 'nccl'],
+                    help='K/V exchange of the gathering path: over peer memory (symmetric buffers, device barrier, '
+                         'one pull launch) or NCCL send/recv (the reference scheme)')
     ap.add_argument('--legs', default=','.join(LEGS),
                     help=f'extra measurements in the line (comma list of {", ".join(LEGS)}; "none" for none)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
@@ -772,8 +786,9 @@ def run_headline(args, dev, rank, world, local):
     # weak scaling: N GPUs run cfg2's scene set repeated N times (per-GPU work about fixed); every scene reads the
     # frame memory of the first copy, so ranks exchange those rows (the path's real K/V gathering step)
     cfg['lengths'] = cfg['lengths'] * world
-    overlap = args.overlap if args.overlap != 'auto' else ('lse' if world >= 4 else 'none')
-    lb = LayerBench(cfg, args.mode, overlap, dev)
+    # the LSE split hides an NCCL exchange from 4 GPUs up; the peer-memory pull is short and runs before attention
+    overlap = args.overlap if args.overlap != 'auto' else ('lse' if world >= 4 and args.exchange == 'nccl' else 'none')
+    lb = LayerBench(cfg, args.mode, overlap, dev, args.exchange)
     t = lb.time(args.warmup, args.steps)
     ms, attn_ms_max = reduce([t['ms'], t['attn_ms']], 'max')
     total_flops, = reduce([t['rank_flops']], 'sum')
@@ -794,6 +809,9 @@ def run_headline(args, dev, rank, world, local):
     if 'kernels' in legs and world == 1:
         extra['hbm_kernels'] = kernels_leg(lb, dev)
     run_mode, path, own = lb.ctx.run_mode, lb.ctx.path, lb.ctx.own
+    from onereel_b200 import comm as _comm
+    exch = ('peer memory (symmetric buffers, device barrier, TMA bulk pull)'
+            if args.exchange == 'peer' and _comm.PEER_UNAVAILABLE is None else 'NCCL send/recv')
     layout = dict(cfg, scenes=lb.lay.n_scenes)
     del lb
     torch.cuda.empty_cache()
@@ -831,7 +849,7 @@ def run_headline(args, dev, rank, world, local):
                 value_per_gpu=total_flops / (ms * 1e-3) / 1e12 / world,
                 config=dict(workload=(f'{args.workload}: one HunyuanVideo-1.5-shaped scene-attention layer through '
                                       'hunyuan15.Processor (pack K/V + attention' +
-                                      (', K/V exchange over NCCL' if world > 1 else '') + ')'),
+                                      (f', K/V exchange over {exch}' if world > 1 else '') + ')'),
                             layout=layout, run_mode=run_mode, path=path, overlap=overlap, own=own,
                             useful_tflop_per_step=total_flops / 1e12,
                             useful_tflop_per_gpu=total_flops / 1e12 / world,

@@ -135,7 +135,8 @@ ORL_API long long orl_pack_prepare(orl_copy_run* runs, const int64_t* nbytes, in
  * dst_bases[p * n_slots + slot]. TMA bulk copies staged through shared memory, HBM-bound. When cu_out_dev is not
  * NULL, also writes cu_seqlens: cu_out_dev[0 .. n_seg] = [0, cumsum(seg_len_dev)] (int32, attention.py:28-29).
  * err_dev (optional device int): a bounded wait that gave up ORs its bit in (see orl_error_bits_describe).
- * At most 8 slots and 3 planes. */
+ * At most 16 slots and 3 planes. Sources may be another GPU's memory mapped into this process (symmetric memory
+ * of the K/V exchange): the bulk loads carry no multicast. */
 ORL_API int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long total_vecs, int n_planes, int n_slots,
              const void* const* src_bases, void* const* dst_bases, const int32_t* seg_len_dev, int n_seg,
              int32_t* cu_out_dev, int* err_dev, void* stream);
@@ -167,6 +168,14 @@ ORL_API int orl_qk_norm_rope(const void* x, void* y, const void* weight, const f
  * (fp32 [n_rows, rope_ld], pair i by cos[2i], sin[2i + sin_shift]). */
 ORL_API int orl_rope_rows(void* x, const int32_t* rows, long long n_rows, int heads, int head_dim, const float* cos_t,
                           const float* sin_t, long long rope_ld, int sin_shift, void* stream);
+
+/* Device barrier of the peer-memory K/V exchange (replaces the synchronisation NCCL's send/recv gives the
+ * reference's HaloExchange, parallel/comm.py:126-201): pads[p] = rank p's signal pad (int[world] in symmetric memory,
+ * zeroed before first use; peer addresses valid in this process). Writes epoch into slot `rank` of every pad, then
+ * waits until every slot of pads[rank] holds at least epoch; epochs must grow by one per call. After timeout_ns the
+ * wait gives up and ORs its bit into err_dev (no hang). world <= 16. */
+ORL_API int orl_peer_barrier(int* const* pads, int world, int rank, int epoch, unsigned long long timeout_ns,
+                             int* err_dev, void* stream);
 
 /* ---------------------------------------------------------------- frame memory (src/onereel/frame_memory.py) */
 

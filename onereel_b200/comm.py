@@ -195,6 +195,30 @@ def exchange_plan(layout, own, T: int, extra=()):
     return need, common, p2p
 
 
+PEER_UNAVAILABLE = None       # why the peer-memory exchange could not be set up in this process (then NCCL is used)
+
+
+def kv_exchange(kind, layout, own, T, k, v, extra=()):
+    """the layer's K/V exchange: over peer memory (kind 'peer': symmetric buffers, a device barrier and one pull
+    launch, onereel_b200.peer) or NCCL send/recv (kind 'nccl': HaloExchange, the reference's scheme). Both deliver
+    the same receive buffers bit for bit. If symmetric memory cannot be set up, the NCCL path is used and the reason
+    kept in PEER_UNAVAILABLE."""
+    global PEER_UNAVAILABLE
+    if kind == 'peer' and PEER_UNAVAILABLE is None:
+        from onereel_b200 import peer
+        try:
+            return peer.PeerExchange(layout, own, T, k, v, extra)
+        except (RuntimeError, AttributeError, NotImplementedError) as e:
+            if peer.initialised():
+                raise
+            PEER_UNAVAILABLE = f'{type(e).__name__}: {e}'
+            import warnings
+            warnings.warn(f'peer-memory K/V exchange unavailable, using NCCL: {PEER_UNAVAILABLE}')
+    elif kind not in ('peer', 'nccl'):
+        raise ValueError(f'exchange must be peer or nccl, got {kind!r}')
+    return HaloExchange(layout, own, T, k, v, extra)
+
+
 class HaloExchange:
     """comm.py:126-201. Posts the K/V exchange of one layer: rank r receives the tokens it reads from their owners and
     sends every peer the tokens of its range that the peer reads. Received intervals land back to back in one buffer

@@ -33,6 +33,7 @@ extern "C" int orl_error_bits_describe(int bits, char* buf, int cap) {
       {orl::kErrTimeoutDrain, "wind-down timed out waiting for in-flight copies"},
       {orl::kErrTimeoutPack, "pack kernel timed out waiting for a bulk copy"},
       {orl::kErrPlan, "cu_seqlens rejected on the device (decreasing or outside the tensors): nothing computed"},
+      {orl::kErrPeerTimeout, "a peer GPU did not reach the device barrier in time"},
   };
   int n = 0;
   for (const auto& e : names)

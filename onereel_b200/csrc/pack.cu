@@ -25,7 +25,7 @@ constexpr int kPackLag = 3;                          // stores trail loads by th
 constexpr int kPackStage = 32 * 1024;                // bytes per piece / shared-memory stage
 constexpr long long kPackTile = 256 * 1024;          // bytes per grid-stride tile
 constexpr int kPackSmem = kPackStages * kPackStage + kPackStages * 8 + 16;
-constexpr int kMaxSlots = 8;
+constexpr int kMaxSlots = 16;                     // e.g. one per peer GPU of an exchange plus locals
 constexpr int kMaxPlanes = 3;
 static_assert(kPackLag < kPackStages, "a stage must be stored before it is reloaded");
 

@@ -22,6 +22,7 @@ enum ErrorBits : int {
   kErrTimeoutDrain = 8,     // wind-down gave up waiting for in-flight copies
   kErrTimeoutPack = 16,     // pack kernel gave up waiting for a bulk load
   kErrPlan = 32,            // the device planner rejected cu_seqlens (decreasing or out of range): nothing computed
+  kErrPeerTimeout = 64,     // a peer did not reach the device barrier in time
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

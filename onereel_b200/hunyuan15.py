@@ -44,6 +44,7 @@ class Context:
     kv_chunks: int = 1
     overlap: str = 'none'
     text_sync: str = 'rows'
+    exchange: str = 'peer'      # B200: K/V exchange over peer memory ('peer') or NCCL send/recv ('nccl')
     memory: int = 0
     frame_memory: object = None
     subject_links: int = 0
@@ -362,9 +363,10 @@ class Processor:
         lse_overlap = ctx.overlap == 'lse'
         plan = self._plan(H, Dh, q.device, lse_overlap)
         _mark('start')
-        ex = comm.HaloExchange(ctx.layout, ctx.own, ctx.T, k, v) if D.world() > 1 else None
+        ex = comm.kv_exchange(ctx.exchange, ctx.layout, ctx.own, ctx.T, k, v) if D.world() > 1 else None
         if ex is not None and ex.remote_index != plan.remote_index:
             raise RuntimeError('exchange layout differs from the compiled plan')
+        _mark('exchange')         # posted (NCCL) or done on this stream (peer memory: copy-in, barrier, pull)
         if _move_active(ctx) and plan.lse:
             raise NotImplementedError("overlap='lse' with shared_pos='adjacent' is not on the B200 path")
         ov, ot = torch.empty_like(q), torch.zeros_like(eq)

@@ -1,0 +1,147 @@
+"""K/V exchange over peer memory on NVLink / NVSwitch — the B200 replacement for the NCCL send/recv of the reference's
+HaloExchange (src/onereel/parallel/comm.py:126-201).
+
+Every rank keeps its own K and V rows of a layer in a symmetric buffer (torch's symmetric memory: one allocation per
+rank, mapped into every peer's address space). A layer's exchange is then, on the compute stream:
+  1. copy the rank's K / V rows into its symmetric buffer (skipped when the producer already wrote them there);
+  2. orl_peer_barrier: a device-side barrier through signal pads in symmetric memory (bounded wait, error bit on
+     timeout) — after it, every rank's rows of this layer have landed;
+  3. one orl_pack launch pulls every interval this rank reads from its owner's buffer (TMA bulk loads from the peer's
+     memory, no multicast) into the receive buffers, K and V as two planes of one run table.
+The receive layout (`remote_index`, `remote_k`, `remote_v`) is HaloExchange's, so the compiled scene plans use either.
+Buffers come in two generations used alternately: a rank rewrites generation g only after the next layer's barrier,
+which every peer reaches after its pull from g in stream order, so one barrier per layer suffices. Symmetric memory
+is allocated without NVLink multicast objects (plain peer mappings only).
+
+Bit-exact with the NCCL path (the rows move unchanged). world == 1 needs no exchange.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import torch
+
+from onereel_b200 import _lib as L
+from onereel_b200 import dist as D
+from onereel_b200.pack import RunTable
+
+# a peer that does not reach the barrier within this time ends the step with an error bit instead of a hang
+BARRIER_TIMEOUT_NS = 2_000_000_000
+
+
+class PeerSpace:
+    """symmetric K/V buffers of `rows` rows x `row_elems` elements (two generations) and the signal pad, on every rank
+    of the process group; the same shape must be requested on every rank (collective)"""
+
+    def __init__(self, rows: int, row_elems: int, dtype: torch.dtype, device: torch.device):
+        os.environ.setdefault('TORCH_SYMM_MEM_DISABLE_MULTICAST', '1')
+        from torch.distributed import _symmetric_memory as symm
+        g = D.group()
+        if hasattr(symm, 'enable_symm_mem_for_group') and hasattr(g, 'group_name'):
+            try:
+                symm.enable_symm_mem_for_group(g.group_name)
+            except Exception:        # already enabled, or enabled implicitly by this torch version
+                pass
+        self.n, self.r = D.world(), D.rank()
+        self.rows, self.row_elems, self.dtype, self.device = rows, row_elems, dtype, torch.device(device)
+        self.row_bytes = row_elems * torch.tensor([], dtype=dtype).element_size()
+        self.gens = []
+        for _ in range(2):
+            buf = symm.empty((2, rows, row_elems), dtype=dtype, device=self.device)
+            h = symm.rendezvous(buf, g)
+            self.gens.append((buf, [int(p) for p in h.buffer_ptrs], h))
+        pad = symm.empty(self.n, dtype=torch.int32, device=self.device)
+        pad.zero_()
+        ph = symm.rendezvous(pad, g)
+        self.pad, self.pad_handle = pad, ph
+        self.pad_ptrs = (ctypes.c_void_p * self.n)(*[int(p) for p in ph.buffer_ptrs])
+        self.epoch, self.gen = 0, 0
+        torch.cuda.synchronize(self.device)
+        D.barrier()                  # every pad zeroed before any rank signals
+
+    def next_gen(self):
+        """the generation this layer writes (alternating)"""
+        g = self.gen
+        self.gen ^= 1
+        return g
+
+    def barrier(self, stream, err_dev):
+        self.epoch += 1
+        L.check(L.lib().orl_peer_barrier(self.pad_ptrs, self.n, self.r, self.epoch, BARRIER_TIMEOUT_NS,
+                                         err_dev.data_ptr(), stream.cuda_stream), 'orl_peer_barrier')
+
+
+_SPACES = {}
+
+
+def initialised() -> bool:
+    """whether a symmetric space exists (a failure after that is an error, not an unavailable feature)"""
+    return bool(_SPACES)
+
+
+def space_for(rows: int, row_elems: int, dtype, device) -> PeerSpace:
+    """one PeerSpace per (shape, dtype, device), created collectively on first use and kept (layers reuse it)"""
+    key = (rows, row_elems, dtype, str(device))
+    sp = _SPACES.get(key)
+    if sp is None:
+        sp = _SPACES[key] = PeerSpace(rows, row_elems, dtype, device)
+    return sp
+
+
+class PeerExchange:
+    """one layer's K/V exchange over peer memory, with HaloExchange's result interface (remote_index, remote_k,
+    remote_v, wait). own: every rank's token range; k / v: this rank's rows [b - a, H, D] (contiguous)."""
+
+    def __init__(self, layout, own, T, k, v, extra=()):
+        from onereel_b200 import attention as A, comm
+        n, r = D.world(), D.rank()
+        self.a, self.b = own[r]
+        self.remote_index, self.remote_k, self.remote_v = [], None, None
+        self.bytes_in = 0
+        if n == 1:
+            return
+        H, Dh = k.shape[1:]
+        rows_max = max(b - a for a, b in own)
+        sp = space_for(rows_max, H * Dh, k.dtype, k.device)
+        rb = sp.row_bytes
+        need, _, _ = comm.exchange_plan(layout, own, T, extra)
+        recv = [(p, lo, hi) for p in range(n) if p != r for lo, hi in comm.clip(need[r], *own[p])]
+        rows = sum(hi - lo for _, lo, hi in recv)
+        self.remote_k = k.new_empty((rows, H, Dh))
+        self.remote_v = v.new_empty((rows, H, Dh))
+        src_slot, src_off, dst_off, nbytes = [], [], [], []
+        off = 0
+        for p, lo, hi in sorted(recv, key=lambda x: x[1]):
+            self.remote_index.append((lo, hi, off))
+            src_slot.append(p)
+            src_off.append((lo - own[p][0]) * rb)
+            dst_off.append(off * rb)
+            nbytes.append((hi - lo) * rb)
+            off += hi - lo
+        self.bytes_in = 2 * off * rb
+        stream = torch.cuda.current_stream(k.device)
+        g = sp.next_gen()
+        buf, ptrs, _ = sp.gens[g]
+        nr = self.b - self.a
+        buf[0, :nr].copy_(k.reshape(nr, H * Dh))
+        buf[1, :nr].copy_(v.reshape(nr, H * Dh))
+        sp.barrier(stream, A._err_word(k.device))
+        if not nbytes:
+            return
+        key = (tuple(map(tuple, own)), tuple(self.remote_index), rb)
+        table = _TABLES.get(key)
+        if table is None:
+            table = _TABLES[key] = RunTable(np.array(src_slot, np.int32), np.full(len(src_slot), n, np.int32),
+                                            src_off, dst_off, nbytes, k.device)
+        plane = sp.rows * rb                       # V follows K in every rank's buffer
+        src = [ptrs[p] for p in range(n)] + [0] + [ptrs[p] + plane for p in range(n)] + [0]
+        dst = [0] * n + [self.remote_k.data_ptr()] + [0] * n + [self.remote_v.data_ptr()]
+        table.run(src, dst, n_planes=2, stream=stream.cuda_stream)
+
+    def wait(self, timeout_s=None):
+        """the pull ran on the compute stream: nothing to wait for"""
+
+
+_TABLES = {}

@@ -145,7 +145,7 @@ class Processor:
                                        q.device) if g else None
             plans = ctx._cache[key] = (rindex, mk(near), mk(far))
         rindex, near, far = plans
-        ex = comm.HaloExchange(lay, ctx.own, T, k, v) if D.world() > 1 else None
+        ex = comm.kv_exchange(getattr(ctx, 'exchange', 'peer'), lay, ctx.own, T, k, v) if D.world() > 1 else None
         if ex is not None and ex.remote_index != rindex:
             raise RuntimeError('exchange layout differs from the compiled plan')
         ov = torch.empty_like(q)

@@ -4,8 +4,9 @@
 Every rank builds the same full tensors from a seeded CPU generator, keeps its partition's rows and runs the parallel
 path; the single-GPU result of the same layer is computed on every rank from the full tensors. Checks (the reference's
 tests/dist_onereel_kv_chunks.py, dist_onereel_overlap.py, dist_onereel_gather.py):
-  - K/V gathering (Hunyuan and Wan) equals the single-GPU result of the same key order bit for bit (video rows and
-    the text rows of the scenes the rank touches), with halo and frame-memory frames, boundaries inside frames; Wan's
+  - K/V gathering (Hunyuan and Wan; the exchange over peer memory, for Hunyuan also over NCCL) equals the
+    single-GPU result of the same key order bit for bit (video rows and the text rows of the scenes the rank
+    touches), with halo and frame-memory frames, boundaries inside frames; Wan's
     one-GPU `ranges` reads the same keys in token order, so it is compared within rel 1e-2;
   - overlap='lse' (local keys during the exchange, LSE merge) within rel 1e-2 of waiting;
   - Ulysses equals the single-GPU result bit for bit; text_sync='all_reduce' equals 'rows' on touched scenes;
@@ -67,6 +68,11 @@ def main():
                 ctx = HY.Context(lay, T=T, own=own, counts={True: counts}, fwd=1, overlap=overlap, text_sync=sync)
                 res[overlap, sync] = HY.Processor(ctx, 0).scene(ql, kl, vl, eq, ek, ev)
         hv, ht = res['none', 'rows']
+        # the K/V exchange over NCCL send/recv (the reference's scheme) moves the same rows as the peer-memory pull
+        nctx = HY.Context(lay, T=T, own=own, counts={True: counts}, fwd=1, exchange='nccl')
+        nv, nt = HY.Processor(nctx, 0).scene(ql, kl, vl, eq, ek, ev)
+        assert torch.equal(nv, hv) and torch.equal(nt[trows], ht[trows]), (lengths, r, 'nccl vs peer exchange')
+        assert comm.PEER_UNAVAILABLE is None, comm.PEER_UNAVAILABLE
         assert torch.equal(hv, ref_v[a:b]), (lengths, r, 'hunyuan video')
         assert torch.equal(ht[trows], ref_t[trows]), (lengths, r, 'hunyuan text')
         assert torch.equal(res['none', 'all_reduce'][1], ref_t), (lengths, r, 'all_reduce text')

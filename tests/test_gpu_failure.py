@@ -28,3 +28,28 @@ def test_bounded_wait_times_out_with_status_and_context_survives():
     ref = torch.nn.functional.scaled_dot_product_attention(*(x.float().transpose(0, 1)[None] for x in (q, k, v)))
     assert (o.float() - ref[0].transpose(0, 1)).abs().max().item() < 2e-2
     assert _lib.lib().orl_selftest_timeout(status.data_ptr(), 0, None) == -1          # invalid limit rejected
+
+
+def test_peer_barrier_times_out_when_a_peer_never_arrives():
+    """the device barrier of the peer-memory exchange, with two signal pads on this one GPU standing for a rank and a
+    peer that never signals: the wait runs out after its limit, sets its error bit, and the context stays usable; a
+    barrier whose other slot is already signalled passes"""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a B200')
+    from onereel_b200.csrc.build import build
+    build()
+    from onereel_b200 import _lib
+    pads = torch.zeros(2, 2, dtype=torch.int32, device='cuda')          # pads[p]: rank p's pad of world 2
+    err = torch.zeros(1, dtype=torch.int32, device='cuda')
+    ptrs = (ctypes.c_void_p * 2)(pads[0].data_ptr(), pads[1].data_ptr())
+    s = torch.cuda.current_stream().cuda_stream
+    assert _lib.lib().orl_peer_barrier(ptrs, 2, 0, 1, 20_000_000, err.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    assert err.item() != 0 and 'barrier' in _lib.describe_error_bits(err.item())
+    assert pads[1, 0].item() == 1 and pads[0, 0].item() == 1            # rank 0 signalled every pad
+    err.zero_()
+    pads[0, 1] = 2                                                       # the peer's signal for epoch 2 is there
+    assert _lib.lib().orl_peer_barrier(ptrs, 2, 0, 2, 20_000_000, err.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert _lib.lib().orl_peer_barrier(ptrs, 2, 2, 3, 20_000_000, err.data_ptr(), s) == -1   # rank outside world
