@@ -177,6 +177,15 @@ ORL_API int orl_rope_rows(void* x, const int32_t* rows, long long n_rows, int he
 ORL_API int orl_peer_barrier(int* const* pads, int world, int rank, int epoch, unsigned long long timeout_ns,
                              int* err_dev, void* stream);
 
+/* All-to-all of the Ulysses path by pulls over peer memory (replaces the NCCL all_to_all_single calls of
+ * parallel/comm.py:276-295 a2a_heads / a2a_tokens): for every plane pl < planes (<= 3), peer p < n_peers (<= 16),
+ * row i < rows, copies seg_bytes from src[pl * n_peers + p] + src_row0 + i * src_stride to
+ * dst[pl] + p * dst_pstride + i * dst_stride. src may be other GPUs' memory mapped into this process (symmetric
+ * buffers, after orl_peer_barrier). Offsets, strides and sizes multiples of 16 bytes. */
+ORL_API int orl_peer_gather(const void* const* src, void* const* dst, int planes, int n_peers, long long rows,
+                            long long seg_bytes, long long src_row0, long long src_stride, long long dst_pstride,
+                            long long dst_stride, void* stream);
+
 /* ---------------------------------------------------------------- frame memory (src/onereel/frame_memory.py) */
 
 /* Per-frame pooling of one layer's hidden states (frame_memory.py:76-85 `collect`, an index_add_ of the rows into

@@ -69,6 +69,8 @@ SIGNATURES = {
     'orl_pack_prepare': (c_ll, [c_vp, P_I64, c_int]),
     'orl_pack': (c_int, [c_vp, c_int, c_ll, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp]),
     'orl_peer_barrier': (c_int, [ctypes.POINTER(c_vp), c_int, c_int, c_int, ctypes.c_ulonglong, c_vp, c_vp]),
+    'orl_peer_gather': (c_int, [ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int, c_int, c_ll, c_ll, c_ll, c_ll, c_ll,
+                                c_ll, c_vp]),
     'orl_lse_merge': (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_ll, c_int, c_int, c_vp]),
     'orl_lse_merge_acc': (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_ll, c_ll, c_int, c_int, c_vp]),
     'orl_qk_norm_rope': (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_int, c_int, c_int, c_float, c_int, c_ll, c_vp,

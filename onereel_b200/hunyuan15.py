@@ -421,7 +421,21 @@ class Processor:
         n, r, H = D.world(), D.rank(), q.shape[1]
         sl = slice(r * H // n, (r + 1) * H // n)
         _mark('start')
-        qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
+        # over peer memory when every rank holds the same number of tokens (the Ulysses split), else NCCL
+        sizes = {b - a for a, b in ctx.own} if ctx.own else {q.shape[0]}
+        use_peer = (ctx.exchange == 'peer' and n > 1 and len(sizes) == 1 and H % n == 0 and
+                    ctx.attn_override is None and comm.PEER_UNAVAILABLE is None)
+        if use_peer:
+            from onereel_b200 import peer
+            try:
+                qa, ka, va = peer.a2a_heads_qkv(q, k, v)
+            except (RuntimeError, AttributeError, NotImplementedError) as e:
+                if peer.initialised():
+                    raise
+                comm.PEER_UNAVAILABLE = f'{type(e).__name__}: {e}'
+                use_peer = False
+        if not use_peer:
+            qa, ka, va = comm.a2a_heads(q), comm.a2a_heads(k), comm.a2a_heads(v)
         eqs, eks, evs = (x[:, sl].contiguous() for x in (eq, ek, ev))
         _mark('a2a_in')
         if ctx.attn_override is not None:
@@ -441,7 +455,10 @@ class Processor:
             plan = ctx._cache[key] = S.ScenePlan(
                 S.scene_segments(lay, T, ctx.counts[ctx.cond()], scenes, set(range(lay.n_scenes)), (0, L)),
                 Hl * Dh * 2, Hl, q.device)
-        ov = torch.empty_like(qa)
+        if use_peer:
+            ov, handle = peer.out_buffer(qa.shape[0], Hl, Dh, qa.dtype, qa.device)
+        else:
+            ov = torch.empty_like(qa)
         otl = torch.zeros_like(eqs)
         _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl, ctx=ctx)
         _mark('attention')
@@ -449,7 +466,7 @@ class Processor:
         ot[:, sl] = otl
         D.all_reduce(ot)
         _mark('text_sync')
-        out = comm.a2a_tokens(ov)
+        out = peer.a2a_tokens_from(ov, handle) if use_peer else comm.a2a_tokens(ov)
         _mark('a2a_out')
         return out, ot
 

@@ -35,7 +35,7 @@ class PeerSpace:
     """symmetric K/V buffers of `rows` rows x `row_elems` elements (two generations) and the signal pad, on every rank
     of the process group; the same shape must be requested on every rank (collective)"""
 
-    def __init__(self, rows: int, row_elems: int, dtype: torch.dtype, device: torch.device):
+    def __init__(self, rows: int, row_elems: int, dtype: torch.dtype, device: torch.device, planes: int = 2):
         os.environ.setdefault('TORCH_SYMM_MEM_DISABLE_MULTICAST', '1')
         from torch.distributed import _symmetric_memory as symm
         g = D.group()
@@ -46,10 +46,11 @@ class PeerSpace:
                 pass
         self.n, self.r = D.world(), D.rank()
         self.rows, self.row_elems, self.dtype, self.device = rows, row_elems, dtype, torch.device(device)
+        self.planes = planes
         self.row_bytes = row_elems * torch.tensor([], dtype=dtype).element_size()
         self.gens = []
         for _ in range(2):
-            buf = symm.empty((2, rows, row_elems), dtype=dtype, device=self.device)
+            buf = symm.empty((planes, rows, row_elems), dtype=dtype, device=self.device)
             h = symm.rendezvous(buf, g)
             self.gens.append((buf, [int(p) for p in h.buffer_ptrs], h))
         pad = symm.empty(self.n, dtype=torch.int32, device=self.device)
@@ -81,12 +82,13 @@ def initialised() -> bool:
     return bool(_SPACES)
 
 
-def space_for(rows: int, row_elems: int, dtype, device) -> PeerSpace:
-    """one PeerSpace per (shape, dtype, device), created collectively on first use and kept (layers reuse it)"""
-    key = (rows, row_elems, dtype, str(device))
+def space_for(rows: int, row_elems: int, dtype, device, planes: int = 2, tag: str = 'kv') -> PeerSpace:
+    """one PeerSpace per (use, planes, shape, dtype, device), created collectively on first use and kept (layers
+    reuse it)"""
+    key = (tag, planes, rows, row_elems, dtype, str(device))
     sp = _SPACES.get(key)
     if sp is None:
-        sp = _SPACES[key] = PeerSpace(rows, row_elems, dtype, device)
+        sp = _SPACES[key] = PeerSpace(rows, row_elems, dtype, device, planes)
     return sp
 
 
@@ -145,3 +147,63 @@ class PeerExchange:
 
 
 _TABLES = {}
+
+
+# ------------------------------------------------------------------------------------------------ Ulysses
+# The all-to-alls of the Ulysses path (the reference's a2a_heads / a2a_tokens, parallel/comm.py:276-295) as pulls
+# over peer memory: q / k / v of every rank go into a three-plane symmetric buffer; after a barrier each rank pulls
+# its heads of every peer's tokens straight into [all tokens, local heads, D]; the attention writes its output into
+# a symmetric buffer, and after a second barrier each rank pulls its tokens of every peer's heads straight into
+# [local tokens, all heads, D]. Generations alternate per call as for the K/V exchange.
+
+def _elem(dtype) -> int:
+    return torch.tensor([], dtype=dtype).element_size()
+
+
+def _gather(src, dst, planes, n, rows, seg, src_row0, src_stride, dst_pstride, dst_stride, stream):
+    S = ctypes.c_void_p * len(src)
+    Dd = ctypes.c_void_p * len(dst)
+    L.check(L.lib().orl_peer_gather(S(*src), Dd(*dst), planes, n, rows, seg, src_row0, src_stride, dst_pstride,
+                                    dst_stride, stream.cuda_stream), 'orl_peer_gather')
+
+
+def a2a_heads_qkv(q, k, v):
+    """[S / N, H, D] x 3 (this rank's tokens, all heads) -> [S, H / N, D] x 3 (all tokens, this rank's heads)"""
+    from onereel_b200 import attention as A
+    n, r = D.world(), D.rank()
+    rows, H, Dh = q.shape
+    Hl, es = H // n, _elem(q.dtype)
+    sp = space_for(rows, H * Dh, q.dtype, q.device, planes=3, tag='ulysses_in')
+    stream = torch.cuda.current_stream(q.device)
+    buf, ptrs, _ = sp.gens[sp.next_gen()]
+    for pl, x in enumerate((q, k, v)):
+        buf[pl].copy_(x.reshape(rows, H * Dh))
+    sp.barrier(stream, A._err_word(q.device))
+    outs = [q.new_empty(n * rows, Hl, Dh) for _ in range(3)]
+    plane = rows * H * Dh * es
+    seg = Hl * Dh * es
+    _gather([ptrs[p] + pl * plane for pl in range(3) for p in range(n)], [o.data_ptr() for o in outs], 3, n, rows,
+            seg, r * seg, H * Dh * es, rows * seg, seg, stream)
+    return outs
+
+
+def out_buffer(total_rows, Hl, Dh, dtype, device):
+    """the attention output of this rank's heads [S, H / N, D] in symmetric memory (this call's generation)"""
+    sp = space_for(total_rows, Hl * Dh, dtype, device, planes=1, tag='ulysses_out')
+    g = sp.next_gen()
+    return sp.gens[g][0][0].view(total_rows, Hl, Dh), (sp, g)
+
+
+def a2a_tokens_from(ov, handle):
+    """[S, H / N, D] in symmetric memory (out_buffer) -> [S / N, H, D]: this rank's tokens of every rank's heads"""
+    from onereel_b200 import attention as A
+    sp, g = handle
+    n, r = D.world(), D.rank()
+    total, Hl, Dh = ov.shape
+    rows, H, es = total // n, Hl * n, _elem(ov.dtype)
+    stream = torch.cuda.current_stream(ov.device)
+    sp.barrier(stream, A._err_word(ov.device))
+    out = ov.new_empty(rows, H, Dh)
+    seg = Hl * Dh * es
+    _gather(sp.gens[g][1], [out.data_ptr()], 1, n, rows, seg, r * rows * seg, seg, seg, H * Dh * es, stream)
+    return out

@@ -9,7 +9,8 @@ tests/dist_onereel_kv_chunks.py, dist_onereel_overlap.py, dist_onereel_gather.py
     touches), with halo and frame-memory frames, boundaries inside frames; Wan's
     one-GPU `ranges` reads the same keys in token order, so it is compared within rel 1e-2;
   - overlap='lse' (local keys during the exchange, LSE merge) within rel 1e-2 of waiting;
-  - Ulysses equals the single-GPU result bit for bit; text_sync='all_reduce' equals 'rows' on touched scenes;
+  - Ulysses (all-to-alls by pulls over peer memory, and over NCCL) equals the single-GPU result bit for bit;
+    text_sync='all_reduce' equals 'rows' on touched scenes;
   - the Scene-Ring baseline (mode='ring', Hunyuan with text and Wan) within rel 1e-2 of the single-GPU result;
   - the Eq. 2 chooser ('auto') picks a path and reproduces the single-GPU result;
   - the bounded memory (memory = 8, halo-free layouts): K/V gathering with the boundary candidates received equals
@@ -90,6 +91,9 @@ def main():
             uv, ut = HY.Processor(uc, 0).ulysses(*(x[ua:ub].contiguous() for x in (q, k, v)), eq, ek, ev)
             assert torch.equal(uv.contiguous(), ref_v[ua:ub]), (lengths, r, 'ulysses video')
             assert torch.equal(ut, ref_t), (lengths, r, 'ulysses text')
+            ucn = HY.Context(lay, T=T, own=uown, counts={True: counts}, fwd=1, run_mode='ulysses', exchange='nccl')
+            unv, unt = HY.Processor(ucn, 0).ulysses(*(x[ua:ub].contiguous() for x in (q, k, v)), eq, ek, ev)
+            assert torch.equal(unv, uv) and torch.equal(unt, ut), (lengths, r, 'ulysses nccl vs peer')
             wu = WN.Processor(WN.Context(lay, T=T, own=uown), 'self', None, 0)
             wo = comm.a2a_tokens(wu.ranges(*(comm.a2a_heads(x[ua:ub].contiguous()) for x in (q, k, v))))
             assert torch.equal(wo.contiguous(), wref[ua:ub]), (lengths, r, 'wan ulysses')

@@ -126,3 +126,34 @@ def test_lse_merge_kernels_match_oracle(Dh):
         gl = got.cpu().numpy()
         both = np.isfinite(want_l)
         assert np.abs(gl[both] - want_l[both]).max() < 1e-4
+
+
+def test_peer_gather_all_to_all_layouts():
+    """orl_peer_gather (the Ulysses all-to-alls over peer memory) on buffers of this one GPU standing for the peers'
+    symmetric buffers: both directions land every row segment where the NCCL all-to-all puts it"""
+    import ctypes
+    from onereel_b200 import _lib as L
+    n, rows, H, Dh = 4, 37, 8, 64
+    Hl, es = H // n, 2
+    g = torch.Generator(device='cuda').manual_seed(5)
+    src = [torch.randn(3, rows, H * Dh, generator=g, device='cuda').to(torch.bfloat16) for _ in range(n)]
+    s = torch.cuda.current_stream().cuda_stream
+    for r in range(n):
+        outs = [torch.empty(n * rows, Hl, Dh, dtype=torch.bfloat16, device='cuda') for _ in range(3)]
+        seg = Hl * Dh * es
+        S = (ctypes.c_void_p * (3 * n))(*[src[p][pl].data_ptr() for pl in range(3) for p in range(n)])
+        Dd = (ctypes.c_void_p * 3)(*[o.data_ptr() for o in outs])
+        assert L.lib().orl_peer_gather(S, Dd, 3, n, rows, seg, r * seg, H * Dh * es, rows * seg, seg, s) == 0
+        for pl in range(3):
+            want = torch.cat([src[p][pl].view(rows, H, Dh)[:, r * Hl:(r + 1) * Hl] for p in range(n)])
+            assert torch.equal(outs[pl], want)
+    ov = [torch.randn(n * rows, Hl, Dh, generator=g, device='cuda').to(torch.bfloat16) for _ in range(n)]
+    for r in range(n):
+        out = torch.empty(rows, H, Dh, dtype=torch.bfloat16, device='cuda')
+        seg = Hl * Dh * es
+        S = (ctypes.c_void_p * n)(*[x.data_ptr() for x in ov])
+        Dd = (ctypes.c_void_p * 1)(out.data_ptr())
+        assert L.lib().orl_peer_gather(S, Dd, 1, n, rows, seg, r * rows * seg, seg, seg, H * Dh * es, s) == 0
+        want = torch.cat([ov[p][r * rows:(r + 1) * rows] for p in range(n)], dim=1)
+        assert torch.equal(out, want)
+    torch.cuda.synchronize()
