@@ -92,9 +92,40 @@ def space_for(rows: int, row_elems: int, dtype, device, planes: int = 2, tag: st
     return sp
 
 
+def _recv_layout(need_r, own, r):
+    """rank r's receive layout: [(token lo, token hi, buffer row, owner)] sorted by lo (HaloExchange's order)"""
+    from onereel_b200 import comm
+    recv = [(lo, hi, p) for p in range(len(own)) if p != r for lo, hi in comm.clip(need_r, *own[p])]
+    out, off = [], 0
+    for lo, hi, p in sorted(recv):
+        out.append((lo, hi, off, p))
+        off += hi - lo
+    return out, off
+
+
+def _row_of(layout_r, lo):
+    """buffer row of token lo in a receive layout"""
+    for a, b, off, _ in layout_r:
+        if a <= lo < b:
+            return off + lo - a
+    raise KeyError(lo)
+
+
+def _stripes(lo, hi, readers):
+    """[lo, hi) cut into len(readers) nearly equal consecutive stripes, one per reader"""
+    k = len(readers)
+    cuts = [lo + (hi - lo) * i // k for i in range(k + 1)]
+    return [(q, cuts[i], cuts[i + 1]) for i, q in enumerate(readers) if cuts[i] < cuts[i + 1]]
+
+
 class PeerExchange:
     """one layer's K/V exchange over peer memory, with HaloExchange's result interface (remote_index, remote_k,
-    remote_v, wait). own: every rank's token range; k / v: this rank's rows [b - a, H, D] (contiguous)."""
+    remote_v, wait). own: every rank's token range; k / v: this rank's rows [b - a, H, D] (contiguous).
+
+    Rows that every other rank reads (frame-memory frames; `common` of comm.exchange_plan, from 3 ranks up) would
+    make their owner's NVLink egress the bottleneck if every reader pulled them from it. They move in two stages
+    instead: each reader pulls one stripe from the owner into its (symmetric) receive buffer, a second barrier, then
+    each reader pulls the other stripes from the readers that fetched them — the owner sends every row once."""
 
     def __init__(self, layout, own, T, k, v, extra=()):
         from onereel_b200 import attention as A, comm
@@ -108,45 +139,107 @@ class PeerExchange:
         rows_max = max(b - a for a, b in own)
         sp = space_for(rows_max, H * Dh, k.dtype, k.device)
         rb = sp.row_bytes
-        need, _, _ = comm.exchange_plan(layout, own, T, extra)
-        recv = [(p, lo, hi) for p in range(n) if p != r for lo, hi in comm.clip(need[r], *own[p])]
-        rows = sum(hi - lo for _, lo, hi in recv)
-        self.remote_k = k.new_empty((rows, H, Dh))
-        self.remote_v = v.new_empty((rows, H, Dh))
-        src_slot, src_off, dst_off, nbytes = [], [], [], []
-        off = 0
-        for p, lo, hi in sorted(recv, key=lambda x: x[1]):
-            self.remote_index.append((lo, hi, off))
-            src_slot.append(p)
-            src_off.append((lo - own[p][0]) * rb)
-            dst_off.append(off * rb)
-            nbytes.append((hi - lo) * rb)
-            off += hi - lo
-        self.bytes_in = 2 * off * rb
+        key = (tuple(map(tuple, own)), T, tuple(layout.lengths), layout.halo, layout.sides,
+               tuple(sorted((j, tuple(f)) for j, f in (layout.extra or {}).items())), tuple(extra), rb)
+        plan = _PLANS.get(key)
+        if plan is None:
+            plan = _PLANS[key] = _Plan(layout, own, T, extra, r, k.device, rb)
+        self.remote_index = plan.remote_index
+        rsp = space_for(max(plan.remote_rows, 1), H * Dh, k.dtype, k.device, tag='kv_remote') if plan.two_stage \
+            else None
         stream = torch.cuda.current_stream(k.device)
         g = sp.next_gen()
         buf, ptrs, _ = sp.gens[g]
+        if rsp is not None:
+            rg = rsp.next_gen()
+            rbuf, rptrs, _ = rsp.gens[rg]
+            self.remote_k = rbuf[0, :plan.rows].view(plan.rows, H, Dh)
+            self.remote_v = rbuf[1, :plan.rows].view(plan.rows, H, Dh)
+        else:
+            self.remote_k = k.new_empty((plan.rows, H, Dh))
+            self.remote_v = v.new_empty((plan.rows, H, Dh))
         nr = self.b - self.a
         buf[0, :nr].copy_(k.reshape(nr, H * Dh))
         buf[1, :nr].copy_(v.reshape(nr, H * Dh))
-        sp.barrier(stream, A._err_word(k.device))
-        if not nbytes:
-            return
-        key = (tuple(map(tuple, own)), tuple(self.remote_index), rb)
-        table = _TABLES.get(key)
-        if table is None:
-            table = _TABLES[key] = RunTable(np.array(src_slot, np.int32), np.full(len(src_slot), n, np.int32),
-                                            src_off, dst_off, nbytes, k.device)
-        plane = sp.rows * rb                       # V follows K in every rank's buffer
-        src = [ptrs[p] for p in range(n)] + [0] + [ptrs[p] + plane for p in range(n)] + [0]
-        dst = [0] * n + [self.remote_k.data_ptr()] + [0] * n + [self.remote_v.data_ptr()]
-        table.run(src, dst, n_planes=2, stream=stream.cuda_stream)
+        err = A._err_word(k.device)
+        sp.barrier(stream, err)
+        kplane, dst = sp.rows * rb, [0] * n + [self.remote_k.data_ptr()] + [0] * n + [self.remote_v.data_ptr()]
+        if plan.stage1 is not None:            # from the owners: every private interval and this rank's stripes
+            plan.stage1.run([ptrs[p] for p in range(n)] + [0] + [ptrs[p] + kplane for p in range(n)] + [0], dst,
+                            n_planes=2, stream=stream.cuda_stream)
+        if rsp is not None:
+            rsp.barrier(stream, err)           # every reader holds its stripes
+            if plan.stage2 is not None:        # the other stripes, from the readers that fetched them
+                rplane = rsp.rows * rb
+                plan.stage2.run([rptrs[p] for p in range(n)] + [0] + [rptrs[p] + rplane for p in range(n)] + [0], dst,
+                                n_planes=2, stream=stream.cuda_stream)
+        self.bytes_in = 2 * plan.rows * rb
 
     def wait(self, timeout_s=None):
         """the pull ran on the compute stream: nothing to wait for"""
 
 
-_TABLES = {}
+class _Plan:
+    """the run tables of one exchange on rank r (cached per layout): stage 1 pulls from the owners, stage 2 the
+    stripes of common rows from the other readers' receive buffers"""
+
+    def __init__(self, layout, own, T, extra, r, device, rb):
+        from onereel_b200 import comm
+        n = len(own)
+        need, common, _ = comm.exchange_plan(layout, own, T, extra)
+        lay = [_recv_layout(need[q], own, q)[0] for q in range(n)]
+        self.remote_index = [(lo, hi, off) for lo, hi, off, _ in lay[r]]
+        self.rows = sum(hi - lo for lo, hi, _, _ in lay[r])
+        self.remote_rows = max(sum(hi - lo for lo, hi, _, _ in lay[q]) for q in range(n))
+        # common intervals by owner, cut into stripes over the readers
+        stripes = {}                           # (owner, lo, hi) -> [(reader, s_lo, s_hi)]
+        for p in range(n):
+            readers = [q for q in range(n) if q != p]
+            for lo, hi in common[p]:
+                stripes[(p, lo, hi)] = _stripes(lo, hi, readers)
+        self.two_stage = bool(stripes)
+        s1, s2 = [], []                        # (src slot, src row, dst row, rows)
+
+        def from_reader(q, a, b, dst_row):
+            # token rows [a, b) out of reader q's receive buffer, split where q's layout is not contiguous
+            for u, w, off_q, _ in lay[q]:
+                x, y = max(a, u), min(b, w)
+                if x < y:
+                    s2.append((q, off_q + x - u, dst_row + x - a, y - x))
+
+        for lo, hi, off, p in lay[r]:
+            cur = lo
+            mine = sorted((clo, chi, parts) for (cp, clo, chi), parts in stripes.items()
+                          if cp == p and clo < hi and chi > lo)
+            for clo, chi, parts in mine:
+                clo, chi = max(clo, lo), min(chi, hi)
+                if clo > cur:
+                    s1.append((p, cur - own[p][0], off + cur - lo, clo - cur))
+                for q, a, b in parts:
+                    a, b = max(a, clo), min(b, chi)
+                    if a >= b:
+                        continue
+                    if q == r:
+                        s1.append((p, a - own[p][0], off + a - lo, b - a))
+                    else:
+                        from_reader(q, a, b, off + a - lo)
+                cur = max(cur, chi)
+            if cur < hi:
+                s1.append((p, cur - own[p][0], off + cur - lo, hi - cur))
+        self.stage1 = self._table(s1, n, device, rb)
+        self.stage2 = self._table(s2, n, device, rb)
+
+    @staticmethod
+    def _table(runs, n, device, rb):
+        runs = [x for x in runs if x[3] > 0]
+        if not runs:
+            return None
+        return RunTable(np.array([x[0] for x in runs], np.int32), np.full(len(runs), n, np.int32),
+                        [x[1] * rb for x in runs], [x[2] * rb for x in runs], [x[3] * rb for x in runs], device)
+
+
+_PLANS = {}
+
 
 
 # ------------------------------------------------------------------------------------------------ Ulysses
