@@ -412,12 +412,15 @@ class LayerBench:
         ms_max, = reduce([ms], 'max')
         b_in, b_out, tb_in, tb_out = reduce([rows_in * rb, rows_out * rb, t_in * rb // 2, t_out * rb // 2], 'max')
         if kind == 'peer' and comm.PEER_UNAVAILABLE is None:
-            # every reader pulls from the owner: the owner's outgoing bytes count each reader
-            rows_out = sum(hi - lo for q in range(n) if q != r for lo, hi in comm.clip(need[q], *own_all[r]))
-            b_in, b_out = reduce([rows_in * rb, rows_out * rb], 'max')
+            # rows this rank serves: every pull whose source is this rank, in either stage of every rank's plan
+            from onereel_b200 import peer
+            plans = [peer._Plan(lay, own_all, T, (), q, 'cpu', 1) for q in range(n)]
+            served = sum(nb for pl in plans for tab in (pl.stage1, pl.stage2) if tab is not None
+                         for src, nb in zip(tab.src_slot, tab.nbytes_list) if src == r)
+            b_in, b_out = reduce([rows_in * rb, served * rb], 'max')
             note = ('K and V of this rank copied into its symmetric buffer, device barrier, every interval pulled '
-                    'from its owner over NVLink (one TMA bulk-copy launch); bytes per GPU and direction, max over '
-                    'ranks')
+                    'over NVLink (TMA bulk copies); rows every rank reads in two stages (a stripe from the owner, '
+                    'the rest from the other readers); bytes per GPU and direction, max over ranks')
         else:
             kind = 'nccl'
             note = ('grouped NCCL send/recv of K and V plus the broadcast of rows every rank reads; bytes per GPU '

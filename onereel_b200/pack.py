@@ -32,6 +32,10 @@ class RunTable:
         nb = np.ascontiguousarray(nbytes, dtype=np.int64)
         total = L.check(L.lib().orl_pack_prepare(arr.ctypes.data, L.i64p(nb), n), 'orl_pack_prepare')
         self.n_runs, self.total_vecs, self.nbytes = n, int(total), int(nb.sum())
+        # the table as built (host lists), for accounting
+        self.src_slot = [int(x) for x in src_slot]
+        self.src_off, self.dst_off = [int(x) for x in src_off], [int(x) for x in dst_off]
+        self.nbytes_list = nb.tolist()
         self.dev = torch.from_numpy(arr.view(np.uint8)).to(device) if n else None
         self.device = torch.device(device)
 

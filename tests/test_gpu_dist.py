@@ -1,4 +1,5 @@
-"""Multi-GPU parity of the parallel paths (K/V gathering, LSE overlap, Ulysses, Eq. 2 chooser) on 2 GPUs over NCCL,
+"""Multi-GPU parity of the parallel paths (K/V gathering, LSE overlap, Ulysses, Eq. 2 chooser) on 2, 4 and 8 GPUs (peer
+memory and NCCL; from 3 ranks up the peer exchange moves rows every rank reads in two stages),
 run as child processes under torchrun (tests/dist_scene_worker.py). Skipped on a box with fewer than 2 GPUs; the
 host-side logic of the same paths is covered on CPU by test_dist_gloo.py and test_planner_native.py."""
 import os
@@ -20,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize('n', [2])
+@pytest.mark.parametrize('n', [2, 4, 8])
 def test_parallel_paths_match_single_gpu(n):
     if not torch.cuda.is_available() or torch.cuda.device_count() < n:
         pytest.skip(f'needs {n} GPUs')
