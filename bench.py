@@ -257,7 +257,7 @@ class LayerBench:
             D.barrier()
             torch.cuda.synchronize()
             S.TIMING = []
-            packs0 = RunTable.launches
+            packs0, attn0 = RunTable.launches, A.LAUNCHES
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record(self.stream)
             for _ in range(steps):
@@ -271,7 +271,7 @@ class LayerBench:
         timing, S.TIMING = S.TIMING, None
         A.check()
         return dict(ms=t0.elapsed_time(t1) / steps, attn_ms=sum(a.elapsed_time(b) for a, b, _ in timing) / steps,
-                    rank_flops=rank_flops, launches=len(timing) + RunTable.launches - packs0,
+                    rank_flops=rank_flops, launches=A.LAUNCHES - attn0 + RunTable.launches - packs0,
                     clocks=clk.summary() if clk else None)
 
     def attn_alg_bytes(self):
@@ -292,9 +292,12 @@ class LayerBench:
         touches) and (2) fp32 attention on `fp32_rows` evenly spaced query rows of every segment. Reduced over ranks."""
         from onereel_b200 import scene as S
         lay, T, H, Dh = self.lay, self.T, self.H, self.Dh
+        from onereel_b200 import attention as A
         a, b = self.own
+        splits0 = A.SPLITS
         ov, ot = self.step()
         torch.cuda.synchronize()
+        split = A.SPLITS > splits0              # a coarse Ulysses launch took the key split (LSE merge)
         q, k, v, eq, ek, ev = self.full
         L = lay.n_frames * T
         mine, _ = S.pieces(lay, T, self.own)
@@ -331,11 +334,13 @@ class LayerBench:
         mx, fmx = reduce([mx, fmx], 'max')
         sm, n, fsm, fn, frows, rows = reduce([sm, n, fsm, fn, frows, (b - a) + len(trows)], 'sum')
         bit = bool(reduce([1.0 if bit else 0.0], 'min')[0])
-        expect_bit = self.ctx.run_mode == 'ulysses' or not (self.ctx.overlap == 'lse' and self.world > 1)
+        split = bool(reduce([1.0 if split else 0.0], 'max')[0])
+        expect_bit = ((self.ctx.run_mode == 'ulysses' and not split) or
+                      (self.ctx.run_mode != 'ulysses' and not (self.ctx.overlap == 'lse' and self.world > 1)))
         fp32 = dict(max_abs=fmx, mean_abs=fsm / max(fn, 1), rows=int(frows), tolerance=[MAX_ABS, MEAN_ABS])
         ok_fp32 = fmx <= MAX_ABS and fp32['mean_abs'] <= MEAN_ABS
         ok_1gpu = bit if expect_bit else (mx <= MAX_ABS and sm / max(n, 1) <= MEAN_ABS)
-        return dict(path=self.ctx.run_mode, overlap=self.ctx.overlap, ok=bool(ok_fp32 and ok_1gpu),
+        return dict(path=self.ctx.run_mode, overlap=self.ctx.overlap, key_split=split, ok=bool(ok_fp32 and ok_1gpu),
                     one_gpu=dict(bit_exact=bit, expected_bit_exact=expect_bit, max_abs=mx, mean_abs=sm / max(n, 1),
                                  rows=int(rows), what='the rank\'s video rows and the text rows of every scene it '
                                                       'touches, recomputed as one GPU computes them'),

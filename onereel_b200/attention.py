@@ -102,19 +102,74 @@ def _check_inputs(q, k, v):
         raise ValueError(f'head_dim {q.shape[2]} not supported (64 or 128)')
 
 
-def attend(q, k, v, q_start, q_len, k_start, k_len, out=None, lse=None, scale=None, stream=None):
+# Key split of coarse launches (split_keys=True): a launch of fewer than SPLIT_WAVES waves of work items whose longest
+# segment has at least SPLIT_MIN_KEYS keys runs as two launches over the two halves of every segment's keys, on two
+# streams so the second fills the first's tail, merged by log-sum-exp. Exact attention, but another rounding than
+# one pass: callers that promise bit-exact results across partitions (K/V gathering) never ask for it.
+SPLIT_WAVES = 4
+SPLIT_MIN_KEYS = 2048
+LAUNCHES = 0          # attention launches issued by this process (benchmark launch accounting)
+SPLITS = 0            # launches that took the key split
+_SIDE = {}
+_SMS = {}
+
+
+def _sm_count(dev) -> int:
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    if key not in _SMS:
+        _SMS[key] = torch.cuda.get_device_properties(key).multi_processor_count
+    return _SMS[key]
+
+
+def _attend_split(q, k, v, q_start, q_len, k_start, k_len, out, lse, scale):
+    """the two key halves (at a 128-key boundary) on the current and a side stream, then orl_lse_merge"""
+    global SPLITS
+    SPLITS += 1
+    dev = q.device
+    H, Nq = q.shape[1], q.shape[0]
+    half = [128 * ((x + 255) // 256) if x >= 256 else x for x in k_len]
+    cur = torch.cuda.current_stream(dev)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    side = _SIDE.get(key)
+    if side is None:
+        side = _SIDE[key] = torch.cuda.Stream(dev)
+    out = torch.empty_like(q) if out is None else out
+    lse_a = torch.empty(H, Nq, dtype=torch.float32, device=dev) if not isinstance(lse, torch.Tensor) else lse
+    out_b = torch.empty_like(q)
+    lse_b = torch.empty(H, Nq, dtype=torch.float32, device=dev)
+    side.wait_stream(cur)
+    attend(q, k, v, q_start, q_len, k_start, half, out=out, lse=lse_a, scale=scale)
+    with torch.cuda.stream(side):
+        attend(q, k, v, q_start, q_len, [a + h for a, h in zip(k_start, half)], [x - h for x, h in zip(k_len, half)],
+               out=out_b, lse=lse_b, scale=scale, stream=side.cuda_stream)
+    out_b.record_stream(side)
+    lse_b.record_stream(side)
+    cur.wait_stream(side)
+    lse_merge(out, lse_a, out_b, lse_b)
+    return out, (lse_a if lse is not None else None)
+
+
+def attend(q, k, v, q_start, q_len, k_start, k_len, out=None, lse=None, scale=None, stream=None, split_keys=False):
     """the kernel call: segment i = q rows q_start[i] + [0, q_len[i]) attending to k / v rows k_start[i] + [0, k_len[i]).
-    out [Nq, H, D] bf16 (allocated if None); lse None, True (allocate [H, Nq] fp32) or a tensor."""
+    out [Nq, H, D] bf16 (allocated if None); lse None, True (allocate [H, Nq] fp32) or a tensor. split_keys: allow the
+    key split of coarse launches (see SPLIT_WAVES)."""
     _check_inputs(q, k, v)
     Nq, H, Dh = q.shape
     dev = q.device
     work, n = plan(q_start, q_len, k_start, k_len, H, dev)
+    if (split_keys and stream is None and n and n < SPLIT_WAVES * _sm_count(dev) and
+            max(k_len) >= SPLIT_MIN_KEYS):
+        if lse is True:
+            lse = torch.empty(H, Nq, dtype=torch.float32, device=dev)
+        return _attend_split(q, k, v, q_start, q_len, k_start, k_len, out, lse, scale)
     if out is None:
         out = torch.empty_like(q)
     if lse is True:
         lse = torch.empty(H, Nq, dtype=torch.float32, device=dev)
     scale = Dh ** -0.5 if scale is None else float(scale)
     s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    global LAUNCHES
+    LAUNCHES += 1
     L.check(L.lib().orl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                                  None if lse is None else lse.data_ptr(), Nq, k.shape[0], H, Dh, scale,
                                  work.data_ptr(), n, _err_word(dev).data_ptr(), s), 'orl_attn_fwd')

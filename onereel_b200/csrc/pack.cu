@@ -126,12 +126,17 @@ __global__ void __launch_bounds__(32) pack_kernel(const CopyRun* __restrict__ ru
 }
 
 // Merge weights of two partial results by their log-sum-exp (m = max(l1, l2), 0 when both are -inf):
-// a = w1 / (w1 + w2), b = w2 / (w1 + w2) with w_i = exp(l_i - m), and the merged lse m + log(w1 + w2).
+// a = w1 / (w1 + w2), b = w2 / (w1 + w2) with w_i = exp(l_i - m), and the merged lse m + log(w1 + w2); when both
+// parts are empty (lse -inf) the weights are 0 and the lse stays -inf.
 __device__ __forceinline__ float merge_weights(float l1, float l2, float& a, float& b) {
   float m = fmaxf(l1, l2);
   if (isinf(m)) m = 0.f;
   const float w1 = __expf(l1 - m), w2 = __expf(l2 - m);
   const float den = w1 + w2;
+  if (!(den > 0.f)) {            // neither part has a key: zero output, lse -inf (as a segment without keys)
+    a = b = 0.f;
+    return -INFINITY;
+  }
   a = w1 / den;
   b = w2 / den;
   return m + __logf(den);

@@ -45,6 +45,7 @@ class Context:
     overlap: str = 'none'
     text_sync: str = 'rows'
     exchange: str = 'peer'      # B200: K/V exchange over peer memory ('peer') or NCCL send/recv ('nccl')
+    split_keys: bool = True     # B200: Ulysses may split the keys of a coarse launch in two (LSE merge; not bit-exact)
     memory: int = 0
     frame_memory: object = None
     subject_links: int = 0
@@ -245,7 +246,7 @@ class _RankPlan:
             self.far_local = self.far_remote = None
 
 
-def _attend(plan, q, eq, k, v, ek, ev, ov, ot, rk=None, rv=None, lse_v=None, lse_t=None, ctx=None):
+def _attend(plan, q, eq, k, v, ek, ev, ov, ot, rk=None, rv=None, lse_v=None, lse_t=None, ctx=None, split_keys=False):
     if plan is None or not plan.segs:
         return
     kp, vp = plan.pack_kv(k, v, ek, ev, rk, rv)
@@ -253,7 +254,7 @@ def _attend(plan, q, eq, k, v, ek, ev, ov, ot, rk=None, rv=None, lse_v=None, lse
         rot = _shared_rotation(ctx, plan, kp.device)
         if rot is not None:
             rotate_rows(kp, *rot)
-    S.attend_segments(plan, q, eq, kp, vp, ov, ot, lse_v, lse_t)
+    S.attend_segments(plan, q, eq, kp, vp, ov, ot, lse_v, lse_t, split_keys=split_keys)
 
 
 class Processor:
@@ -456,17 +457,30 @@ class Processor:
                 S.scene_segments(lay, T, ctx.counts[ctx.cond()], scenes, set(range(lay.n_scenes)), (0, L)),
                 Hl * Dh * 2, Hl, q.device)
         if use_peer:
-            ov, handle = peer.out_buffer(qa.shape[0], Hl, Dh, qa.dtype, qa.device)
-        else:
-            ov = torch.empty_like(qa)
+            # video and text outputs of this rank's heads in symmetric memory; one barrier, then every rank pulls its
+            # tokens of all heads and all heads of the text rows (no all-reduce)
+            ov, otl, handle = peer.out_buffer(qa.shape[0], Hl, Dh, qa.dtype, qa.device, eqs.shape[0])
+            if otl is not None:
+                otl.zero_()
+            else:
+                otl = torch.zeros_like(eqs)
+            _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl, ctx=ctx, split_keys=ctx.split_keys)
+            _mark('attention')
+            if eqs.shape[0]:
+                out, ot = peer.a2a_tokens_from(ov, handle, otl)
+            else:
+                out, ot = peer.a2a_tokens_from(ov, handle), eq.new_zeros(eq.shape)
+            _mark('a2a_out')
+            return out, ot
+        ov = torch.empty_like(qa)
         otl = torch.zeros_like(eqs)
-        _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl, ctx=ctx)
+        _attend(plan, qa, eqs, ka, va, eks, evs, ov, otl, ctx=ctx, split_keys=ctx.split_keys)
         _mark('attention')
         ot = eq.new_zeros(eq.shape)
         ot[:, sl] = otl
         D.all_reduce(ot)
         _mark('text_sync')
-        out = peer.a2a_tokens_from(ov, handle) if use_peer else comm.a2a_tokens(ov)
+        out = comm.a2a_tokens(ov)
         _mark('a2a_out')
         return out, ot
 

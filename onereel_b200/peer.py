@@ -280,23 +280,36 @@ def a2a_heads_qkv(q, k, v):
     return outs
 
 
-def out_buffer(total_rows, Hl, Dh, dtype, device):
-    """the attention output of this rank's heads [S, H / N, D] in symmetric memory (this call's generation)"""
-    sp = space_for(total_rows, Hl * Dh, dtype, device, planes=1, tag='ulysses_out')
+def out_buffer(total_rows, Hl, Dh, dtype, device, text_rows: int = 0):
+    """the attention outputs of this rank's heads in symmetric memory (this call's generation): video [S, H / N, D]
+    and, when text_rows > 0, text [text_rows, H / N, D] right after it"""
+    sp = space_for(total_rows + text_rows, Hl * Dh, dtype, device, planes=1, tag='ulysses_out')
     g = sp.next_gen()
-    return sp.gens[g][0][0].view(total_rows, Hl, Dh), (sp, g)
+    flat = sp.gens[g][0][0]
+    ov = flat[:total_rows].view(total_rows, Hl, Dh)
+    ot = flat[total_rows:total_rows + text_rows].view(text_rows, Hl, Dh) if text_rows else None
+    return ov, ot, (sp, g, total_rows)
 
 
-def a2a_tokens_from(ov, handle):
-    """[S, H / N, D] in symmetric memory (out_buffer) -> [S / N, H, D]: this rank's tokens of every rank's heads"""
+def a2a_tokens_from(ov, handle, ot=None):
+    """[S, H / N, D] in symmetric memory (out_buffer) -> [S / N, H, D]: this rank's tokens of every rank's heads; with
+    ot (the text outputs of this rank's heads, same buffer) also [text rows, H, D]: every rank's heads of the text
+    rows (what the reference assembles with an all-reduce of head-sliced zeros, hunyuan15.py:279-303). One barrier."""
     from onereel_b200 import attention as A
-    sp, g = handle
+    sp, g, vrows = handle
     n, r = D.world(), D.rank()
     total, Hl, Dh = ov.shape
     rows, H, es = total // n, Hl * n, _elem(ov.dtype)
     stream = torch.cuda.current_stream(ov.device)
     sp.barrier(stream, A._err_word(ov.device))
-    out = ov.new_empty(rows, H, Dh)
     seg = Hl * Dh * es
-    _gather(sp.gens[g][1], [out.data_ptr()], 1, n, rows, seg, r * rows * seg, seg, seg, H * Dh * es, stream)
-    return out
+    ptrs = sp.gens[g][1]
+    out = ov.new_empty(rows, H, Dh)
+    _gather(ptrs, [out.data_ptr()], 1, n, rows, seg, r * rows * seg, seg, seg, H * Dh * es, stream)
+    if ot is None:
+        return out
+    tr = ot.shape[0]
+    text = ot.new_empty(tr, H, Dh)
+    if tr:
+        _gather(ptrs, [text.data_ptr()], 1, n, tr, seg, vrows * seg, seg, seg, H * Dh * es, stream)
+    return out, text

@@ -216,28 +216,47 @@ class ScenePlan:
         return kp, vp
 
 
-# Optional launch timing for benchmarks: when TIMING is a list, every attention launch appends (start, end) CUDA
+# Optional launch timing for benchmarks: when TIMING is a list, every attend_segments call appends (start, end) CUDA
 # events recorded on its stream, with the useful FLOPs it computes.
 TIMING = None
 
 
-def attend_segments(plan: ScenePlan, q, eq, kp, vp, ov, ot, lse_v=None, lse_t=None):
+_TEXT_STREAM = {}
+
+
+def attend_segments(plan: ScenePlan, q, eq, kp, vp, ov, ot, lse_v=None, lse_t=None, split_keys=False):
     """attention of every segment of the plan: queries read in place from q (video) and eq (text). Video outputs go
-    straight to their rows of ov; text outputs straight to their rows of ot. One kernel launch per query source."""
+    straight to their rows of ov; text outputs straight to their rows of ot. One kernel launch per query source; the
+    text launch (a few long items: every sentence attends to its whole scene) runs on a second stream beside the
+    video launch, so its items fill the video launch's last wave instead of running after it (scheduling only: the
+    results are the same bits). split_keys: allow the key split of coarse launches (attention.attend)."""
+    launches = []
     for kind, qsrc, dst, lse in (('v', q, ov, lse_v), ('t', eq, ot, lse_t)):
         idx = [i for i, s in enumerate(plan.segs) if s.kind == kind]
-        if not idx:
-            continue
-        qs = [plan.segs[i].q[1] for i in idx]
-        ql = [plan.segs[i].lq for i in idx]
-        ks = [plan.cu_k[i] for i in idx]
-        kl = [plan.lk[i] for i in idx]
-        if TIMING is not None:
-            stream = torch.cuda.current_stream(qsrc.device)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        A.attend(qsrc, kp, vp, qs, ql, ks, kl, out=dst, lse=lse)
-        if TIMING is not None:
-            e1.record(stream)
-            H, Dh = qsrc.shape[1:]
-            TIMING.append((e0, e1, sum(4.0 * a * b * H * Dh for a, b in zip(ql, kl))))
+        if idx:
+            launches.append((qsrc, dst, lse, [plan.segs[i].q[1] for i in idx], [plan.segs[i].lq for i in idx],
+                             [plan.cu_k[i] for i in idx], [plan.lk[i] for i in idx]))
+    if not launches:
+        return
+    dev = launches[0][0].device
+    cur = torch.cuda.current_stream(dev)
+    if TIMING is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+    if len(launches) == 2:
+        key = dev.index if dev.index is not None else torch.cuda.current_device()
+        side = _TEXT_STREAM.get(key)
+        if side is None:
+            side = _TEXT_STREAM[key] = torch.cuda.Stream(dev)
+        side.wait_stream(cur)
+        qsrc, dst, lse, qs, ql, ks, kl = launches[1]
+        with torch.cuda.stream(side):
+            A.attend(qsrc, kp, vp, qs, ql, ks, kl, out=dst, lse=lse, stream=side.cuda_stream)
+    qsrc, dst, lse, qs, ql, ks, kl = launches[0]
+    A.attend(qsrc, kp, vp, qs, ql, ks, kl, out=dst, lse=lse, split_keys=split_keys)
+    if len(launches) == 2:
+        cur.wait_stream(side)
+    if TIMING is not None:
+        e1.record(cur)
+        H, Dh = launches[0][0].shape[1:]
+        TIMING.append((e0, e1, sum(4.0 * a * b * H * Dh for x in launches for a, b in zip(x[4], x[6]))))

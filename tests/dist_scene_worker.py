@@ -94,6 +94,14 @@ def main():
             ucn = HY.Context(lay, T=T, own=uown, counts={True: counts}, fwd=1, run_mode='ulysses', exchange='nccl')
             unv, unt = HY.Processor(ucn, 0).ulysses(*(x[ua:ub].contiguous() for x in (q, k, v)), eq, ek, ev)
             assert torch.equal(unv, uv) and torch.equal(unt, ut), (lengths, r, 'ulysses nccl vs peer')
+            # the key split of coarse launches (forced here by lowering its threshold): exact within tolerance
+            keep = A.SPLIT_MIN_KEYS
+            A.SPLIT_MIN_KEYS = 0
+            try:
+                sv, st = HY.Processor(uc, 0).ulysses(*(x[ua:ub].contiguous() for x in (q, k, v)), eq, ek, ev)
+            finally:
+                A.SPLIT_MIN_KEYS = keep
+            assert rel(sv, ref_v[ua:ub]) < 1e-2 and rel(st, ref_t) < 1e-2, (lengths, r, 'ulysses key split')
             wu = WN.Processor(WN.Context(lay, T=T, own=uown), 'self', None, 0)
             wo = comm.a2a_tokens(wu.ranges(*(comm.a2a_heads(x[ua:ub].contiguous()) for x in (q, k, v))))
             assert torch.equal(wo.contiguous(), wref[ua:ub]), (lengths, r, 'wan ulysses')

@@ -239,3 +239,25 @@ def test_varlen_device_cu_seqlens_plan_on_gpu(Dh):
     torch.cuda.synchronize()
     with pytest.raises(L.OrlError, match='cu_seqlens rejected'):
         A.check()
+
+
+def test_key_split_of_coarse_launches():
+    """attend(split_keys=True) on a launch of less than a few waves with long segments: the two key halves run on two
+    streams and merge by log-sum-exp — exact attention within the kernel tolerance of fp32 and of the unsplit call;
+    segments too short to split, and a segment without keys, come out as unsplit"""
+    from onereel_b200 import attention as A
+    H, Dh = 2, 128
+    lq, lk = [256, 200, 5, 64], [5000, 2300, 100, 0]
+    q, k, v = rand(sum(lq), H, Dh, seed=21), rand(sum(lk), H, Dh, seed=22), rand(sum(lk), H, Dh, seed=23)
+    qs, ks = np.cumsum([0] + lq)[:-1].tolist(), np.cumsum([0] + lk)[:-1].tolist()
+    splits = A.SPLITS
+    o, l = A.attend(q, k, v, qs, lq, ks, lk, lse=True, split_keys=True)
+    torch.cuda.synchronize()
+    A.check()
+    assert A.SPLITS == splits + 1
+    o1, l1 = A.attend(q, k, v, qs, lq, ks, lk, lse=True)
+    mx, mean, lmx = compare(o, l, ref_attention(q, k, v, qs, lq, ks, lk), qs)
+    assert mx < MAX_ABS and mean < MEAN_ABS and lmx < 1e-3, (mx, mean, lmx)
+    assert (o.float() - o1.float()).abs().max().item() < MAX_ABS
+    assert torch.equal(o[sum(lq[:3]):], torch.zeros_like(o[sum(lq[:3]):]))
+    assert torch.isinf(l[:, sum(lq[:3]):]).all()

@@ -117,6 +117,8 @@ def test_lse_merge_kernels_match_oracle(Dh):
     acc, lacc = d(o1).float().contiguous(), d(l1).contiguous()
     A.lse_merge_acc(acc, lacc, d(o2).contiguous(), d(l2).contiguous())
     torch.cuda.synchronize()
+    # a row where neither part has keys merges to zeros with lse -inf (as a segment without keys)
+    assert torch.equal(g1[11, 2].float().cpu(), torch.zeros(Dh)) and gl1[2, 11].item() == -float('inf')
     fin = ~np.isnan(want_o)
     # bf16 result: within one bf16 rounding (2^-8 relative) of the fp64 merge
     err = np.abs(g1.float().cpu().numpy() - want_o)[fin]
