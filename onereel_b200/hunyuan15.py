@@ -45,7 +45,7 @@ class Context:
     overlap: str = 'none'
     text_sync: str = 'rows'
     exchange: str = 'peer'      # B200: K/V exchange over peer memory ('peer') or NCCL send/recv ('nccl')
-    split_keys: bool = True     # B200: Ulysses may split the keys of a coarse launch in two (LSE merge; not bit-exact)
+    split_keys: bool = False    # B200: Ulysses may split the keys of a coarse launch in two (LSE merge; not bit-exact)
     memory: int = 0
     frame_memory: object = None
     subject_links: int = 0
