@@ -419,8 +419,9 @@ class LayerBench:
         if kind == 'peer' and comm.PEER_UNAVAILABLE is None:
             # rows this rank serves: every pull whose source is this rank, in either stage of every rank's plan
             from onereel_b200 import peer
-            plans = [peer._Plan(lay, own_all, T, (), q, 'cpu', 1) for q in range(n)]
-            served = sum(nb for pl in plans for tab in (pl.stage1, pl.stage2) if tab is not None
+            # (tables built on the host with 16-byte rows, the smallest row the pack accepts; served counts rows)
+            plans = [peer._Plan(lay, own_all, T, (), q, 'cpu', 16) for q in range(n)]
+            served = sum(nb // 16 for pl in plans for tab in (pl.stage1, pl.stage2) if tab is not None
                          for src, nb in zip(tab.src_slot, tab.nbytes_list) if src == r)
             b_in, b_out = reduce([rows_in * rb, served * rb], 'max')
             note = ('K and V of this rank copied into its symmetric buffer, device barrier, every interval pulled '

@@ -50,3 +50,18 @@ def test_two_stage_pull_fills_the_reference_layout(monkeypatch, lengths, memory,
         need, common, p2p = comm.exchange_plan(lay, own, T)
         private = sum(hi - lo for q in range(n) if q != 0 for lo, hi in p2p[(0, q)])
         assert owner_rows == private + sum(hi - lo for lo, hi in common[0])
+
+
+def test_plans_build_real_run_tables_on_the_host():
+    """the bench's accounting builds every rank's plan with real run tables on the host (16-byte rows, the smallest
+    the pack accepts): cfg2's scene set on 8 ranks"""
+    lengths = [8, 6, 10, 7] * 8
+    lay = SceneLayout(lengths, halo=0)
+    lay.extra = {j: [f for f in (0, 8, 14, 24) if not lo <= f < hi] for j, (lo, hi) in enumerate(lay.ranges)}
+    T, n = 1590, 8
+    own = comm.partition(lay, n, T, 'scene', [128] * len(lengths))
+    plans = [P._Plan(lay, own, T, (), q, 'cpu', 16) for q in range(n)]
+    served = [sum(nb // 16 for pl in plans for tab in (pl.stage1, pl.stage2) if tab is not None
+                  for src, nb in zip(tab.src_slot, tab.nbytes_list) if src == r) for r in range(n)]
+    received = [pl.rows for pl in plans]
+    assert sum(served) == sum(received) and all(x > 0 for x in received[1:])
