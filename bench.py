@@ -103,12 +103,25 @@ class Clocks:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.Q}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                          '--format=csv,noheader,nounits', '-lms', '50'],
                                          stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
-        time.sleep(0.3)
+        # the timed region starts once the sampler is running (its first line written; NVML start-up can take
+        # a second on a busy 8-GPU host), so a short region still gets samples
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 10.0:
+            if self.path.exists() and self.path.stat().st_size > 0:
+                break
+            time.sleep(0.05)
+        self.start_lines = self._lines()
         return self
+
+    def _lines(self):
+        try:
+            return len(self.path.read_text().strip().splitlines())
+        except OSError:
+            return 0
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -118,7 +131,11 @@ class Clocks:
     def summary(self):
         if self.proc is None or not self.path.exists():
             return None
-        rows = [r.split(', ') for r in self.path.read_text().strip().splitlines() if r.count(',') >= 8]
+        lines = self.path.read_text().strip().splitlines()
+        # the samples taken while the timed region ran (the lines written before it started are dropped, but the
+        # last of those is kept when the region was shorter than one sampling interval)
+        lines = lines[max(0, getattr(self, 'start_lines', 0) - 1):]
+        rows = [r.split(', ') for r in lines if r.count(',') >= 8]
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
