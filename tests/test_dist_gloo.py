@@ -1,6 +1,7 @@
 """The collectives of the parallel paths on CPU gloo ranks (world size 2 and 3): the K/V exchange lands exactly the
 rows each rank's compiled plan expects (at world 3 rows every peer reads arrive by broadcast), the text-row P2P and the Ulysses all-to-all round trip move the right rows,
-gather_tokens reassembles unequal ranges — the reference's tests/dist_onereel_gather.py checks, without a GPU."""
+gather_tokens reassembles unequal ranges — the reference's tests/dist_onereel_gather.py checks, without a GPU; the
+peer-memory exchange falls back to NCCL-style send/recv where symmetric memory is unavailable."""
 import os
 import socket
 import traceback
@@ -48,6 +49,12 @@ def _worker(rank, world, port, q):
                 if flo * T < b and fhi * T > a:
                     want = torch.cat([k[f * T:(f + 1) * T] for f in lay.key_frames(j)])
                     assert torch.equal(ex.rows(0)(lay.key_frames(j)), want), (lengths, r, j)
+            # the peer-memory exchange needs CUDA symmetric memory: on CPU ranks it falls back to this exchange, with
+            # the reason kept, and delivers the same rows
+            ex2 = comm.kv_exchange('peer', lay, own, T, k[a:b].contiguous(), v[a:b].contiguous())
+            ex2.wait()
+            assert comm.PEER_UNAVAILABLE is not None and isinstance(ex2, comm.HaloExchange)
+            assert ex2.remote_index == ex.remote_index and torch.equal(ex2.remote_k, ex.remote_k)
             kb, vb, token_row = ex.buffer()
             held = token_row >= 0
             assert torch.equal(kb[token_row[held]], k[held])
