@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "orl_common.h"
 #include "ptx.cuh"
@@ -256,12 +257,16 @@ extern "C" int orl_pack(const orl_copy_run* runs_dev, int n_runs, long long tota
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  static bool smem_set[64] = {};                     // the shared-memory opt-in, once per device
+  static std::mutex mu;                              // the shared-memory opt-in, once per device
+  static bool smem_set[64] = {};
   if (dev < 0 || dev >= 64) return ORL_ERR_LAUNCH;
-  if (!smem_set[dev]) {
-    if (cudaFuncSetAttribute(pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmem) != cudaSuccess)
-      return ORL_ERR_LAUNCH;
-    smem_set[dev] = true;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!smem_set[dev]) {
+      if (cudaFuncSetAttribute(pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmem) != cudaSuccess)
+        return ORL_ERR_LAUNCH;
+      smem_set[dev] = true;
+    }
   }
   const long long total_bytes = total_vecs * 16;
   const long long tiles_per_plane = (total_bytes + kPackTile - 1) / kPackTile;
