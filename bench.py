@@ -243,11 +243,27 @@ class LayerBench:
         q, k, v, eq, ek, ev = self.full
         self.inputs = [q[a:b].contiguous(), k[a:b].contiguous(), v[a:b].contiguous(), eq, ek, ev]
         self.stream = torch.cuda.current_stream(dev)
+        self._peer_kv = None
 
     def step(self, inputs=None):
         x = self.inputs if inputs is None else inputs
         if self.ctx.run_mode == 'ulysses':
             return self.proc.ulysses(*x)
+        if inputs is None and self.world > 1 and self.ctx.exchange == 'peer':
+            # the layer's K / V as a producer that writes them into the exchange buffer of the generation the
+            # exchange uses next (both generations hold the same resident inputs, written once)
+            from onereel_b200 import comm, peer
+            if comm.PEER_UNAVAILABLE is None:
+                if self._peer_kv is None:
+                    # before this rank's first barrier on this buffer, so no peer reads it yet
+                    sp = peer.space_for(max(b - a for a, b in self.ctx.own), self.H * self.Dh, x[1].dtype, self.dev)
+                    nr = x[1].shape[0]
+                    for buf, _, _ in sp.gens:
+                        buf[0, :nr].copy_(x[1].reshape(nr, -1))
+                        buf[1, :nr].copy_(x[2].reshape(nr, -1))
+                    self._peer_kv = True
+                kk, vv = peer.kv_inputs(self.ctx.own, self.H, self.Dh, x[1].dtype, self.dev)
+                x = [x[0], kk, vv] + list(x[3:])
         return self.proc.scene(*x)
 
     def release_full(self):

@@ -92,6 +92,18 @@ def space_for(rows: int, row_elems: int, dtype, device, planes: int = 2, tag: st
     return sp
 
 
+def kv_inputs(own, H, Dh, dtype, device):
+    """where a producer writes this rank's K / V rows of the next layer so the exchange need not copy them:
+    (k [b - a, H, D], v [b - a, H, D]) views of the symmetric buffer of the generation the next PeerExchange of this
+    shape uses (collective on first use, like the exchange). Rows written there must not change until that exchange
+    has run; a PeerExchange given other tensors copies them in as usual."""
+    r = D.rank()
+    rows = own[r][1] - own[r][0]
+    sp = space_for(max(b - a for a, b in own), H * Dh, dtype, device)
+    buf = sp.gens[sp.gen][0]
+    return buf[0, :rows].view(rows, H, Dh), buf[1, :rows].view(rows, H, Dh)
+
+
 def _recv_layout(need_r, own, r):
     """rank r's receive layout: [(token lo, token hi, buffer row, owner)] sorted by lo (HaloExchange's order)"""
     from onereel_b200 import comm
@@ -159,8 +171,11 @@ class PeerExchange:
             self.remote_k = k.new_empty((plan.rows, H, Dh))
             self.remote_v = v.new_empty((plan.rows, H, Dh))
         nr = self.b - self.a
-        buf[0, :nr].copy_(k.reshape(nr, H * Dh))
-        buf[1, :nr].copy_(v.reshape(nr, H * Dh))
+        # a producer that wrote this layer's rows straight into the generation's buffer (kv_inputs) saves the copy
+        if k.data_ptr() != buf[0].data_ptr():
+            buf[0, :nr].copy_(k.reshape(nr, H * Dh))
+        if v.data_ptr() != buf[1].data_ptr():
+            buf[1, :nr].copy_(v.reshape(nr, H * Dh))
         err = A._err_word(k.device)
         sp.barrier(stream, err)
         kplane, dst = sp.rows * rb, [0] * n + [self.remote_k.data_ptr()] + [0] * n + [self.remote_v.data_ptr()]
